@@ -1,0 +1,193 @@
+/*
+ * q3s_sampler.h -- C ABI of the B200 (sm_100a) codec-token sampler.
+ *
+ * One call samples one token per row for a batch of streams: the talker's
+ * codebook-0 step, or one / all fifteen code-predictor stages.  The reference
+ * (X-Square-Robot/Qwen3TTS-Streaming) has no standalone sampler API; its
+ * sampler is a sub-graph of the fused TensorRT decode engine, fed by name
+ * through TRTEngine.infer (engine/backend/executor.py:323-453) with the inputs
+ * built in Executor._build_fused_inputs (engine/backend/executor.py:3376-3475).
+ * The entry points below replace those sub-graphs:
+ *
+ *   q3s_sample           scripts/export/talker_unified_modules.py:407-422
+ *                        (codebook 0: suppress -> repetition penalty ->
+ *                        top-k 50 -> /T -> +Gumbel -> argmax -> one-hot count
+ *                        update), scripts/export/utils.py:1178-1193
+ *                        (CodePredictorUnrolled._select_token, one stage), and
+ *                        tools/validation/prefill_compare.py:383-399
+ *                        (_sample_token: the HF processor chain + multinomial,
+ *                        here an inverse-CDF draw from a caller uniform).
+ *   q3s_sample_cp_frame  scripts/export/utils.py:1218-1237 (the 15-stage
+ *                        sampling loop of CodePredictorUnrolled.forward), as
+ *                        one persistent kernel per frame.
+ *
+ * Conventions
+ *   - Every pointer in a descriptor is a DEVICE pointer (except the
+ *     descriptor itself).  NULL per-row parameter arrays fall back to the
+ *     scalar *_default field.
+ *   - Calls are asynchronous on `stream` (a cudaStream_t passed as void*;
+ *     NULL = the legacy default stream), never allocate, never synchronise,
+ *     and are re-entrant: the library keeps no mutable state except a
+ *     per-device SM-count cache and a thread-local error string.
+ *   - Arguments are validated on the host before any CUDA call; a bad
+ *     argument returns Q3S_ERR_INVALID_ARGUMENT and launches nothing.
+ *     q3s_last_error_string() explains the most recent failure of the
+ *     calling thread.
+ *   - Data problems only visible on the device (history ids outside
+ *     [0,vocab), bad offsets, too many candidates) are OR-ed into the
+ *     optional device word `error_word` (Q3S_DEVERR_* bits); the row is still
+ *     sampled with the offending entries ignored.
+ *   - Nothing here faults on purpose: every device-side wait is bounded and
+ *     reports Q3S_DEVERR_WAIT_TIMEOUT instead of hanging.
+ */
+#ifndef Q3S_SAMPLER_H
+#define Q3S_SAMPLER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q3S_ABI_VERSION 1
+#define Q3S_MAX_VOCAB 8192     /* one CTA holds a whole row on chip */
+#define Q3S_MAX_TOPK 1024      /* largest exactly-K candidate set (gumbel mode) */
+#define Q3S_MAX_CP_STAGES 64
+
+typedef enum q3s_status {
+  Q3S_OK = 0,
+  Q3S_ERR_INVALID_ARGUMENT = 1,
+  Q3S_ERR_UNSUPPORTED = 2,
+  Q3S_ERR_CUDA = 3
+} q3s_status;
+
+typedef enum q3s_draw_mode {
+  /* engine graph: exactly-K top-k ordered (value desc, index asc), scores
+   * v/T + gumbel_noise[rank], argmax (lowest rank on ties). */
+  Q3S_DRAW_GUMBEL = 0,
+  /* validation chain: HF top-k (ties at the k-th value kept), top-p (stable
+   * ascending order), softmax, first index with cdf > u * cdf_last. */
+  Q3S_DRAW_ICDF = 1
+} q3s_draw_mode;
+
+typedef enum q3s_dtype { Q3S_DTYPE_F32 = 0, Q3S_DTYPE_BF16 = 1 } q3s_dtype;
+
+/* row_flags bits written per row (optional output) */
+#define Q3S_ROW_DRAW_BOUNDARY 1   /* draw within 1e-6 (relative) of a CDF edge */
+#define Q3S_ROW_TOPP_BOUNDARY 2   /* a top-p cumulative mass within 1e-6 of 1-p */
+#define Q3S_ROW_GREEDY 4          /* argmax path taken */
+#define Q3S_ROW_FALLBACK 8        /* u*total reached the total: last positive id taken */
+
+/* error_word bits (device side, OR-ed) */
+#define Q3S_DEVERR_HISTORY_ID 1        /* history id outside [0,vocab): ignored */
+#define Q3S_DEVERR_OFFSETS 2           /* offsets not monotone / beyond history_len */
+#define Q3S_DEVERR_NO_MASS 4           /* no finite logit survived (id = argmax) */
+#define Q3S_DEVERR_WAIT_TIMEOUT 8      /* a bounded device wait gave up */
+#define Q3S_DEVERR_CANDIDATES 16       /* exactly-K candidate set overflow */
+
+/* One sampling step over B rows (codebook 0, or one code-predictor stage). */
+typedef struct q3s_sample_desc {
+  uint32_t struct_size;        /* = sizeof(q3s_sample_desc) */
+  int32_t mode;                /* q3s_draw_mode */
+  int32_t batch;               /* B >= 0 (0 = no-op) */
+  int32_t vocab;               /* V, 1..Q3S_MAX_VOCAB */
+  int32_t topk;                /* gumbel: K candidates (1..min(V,Q3S_MAX_TOPK));
+                                  icdf: default top-k when top_k == NULL (<=0 or >=V: off) */
+  int32_t logits_dtype;        /* q3s_dtype */
+  int64_t logits_row_stride;   /* elements between rows (>= V) */
+  const void* logits;          /* [B, stride] */
+  const int64_t* col_shift;    /* optional [B]: row b, column v is read at
+                                  logits[b, (v + col_shift[b]) mod V] */
+
+  /* presence history: token_counts layout OR packed ragged layout (or none) */
+  const int64_t* token_counts; /* [B, token_counts_row_stride] int64, count > 0 = appeared */
+  int64_t token_counts_row_stride;
+  const int32_t* history;      /* packed ids; row b = history[offsets[b] .. offsets[b+1]) */
+  const int32_t* offsets;      /* [B+1] */
+  int64_t history_len;         /* entries in `history` (bounds check) */
+
+  /* per-row parameters (NULL = scalar default) */
+  const float* temperature;    float temperature_default;   /* icdf: <= 0 = greedy */
+  const int32_t* top_k;        /* icdf only; NULL = `topk` for every row */
+  const float* top_p;          float top_p_default;         /* icdf: >= 1 = off */
+  const float* penalty;        float penalty_default;       /* 1 = off */
+  const int32_t* min_new_tokens; int32_t min_new_tokens_default;
+  const int32_t* cur_len;      /* NULL: history length (packed) or 0 */
+
+  /* randomness, supplied by the caller */
+  const float* gumbel_noise;   /* gumbel: [B, gumbel_row_stride], column r pairs with rank r;
+                                  NULL = greedy argmax over the full row (utils.py:1185-1186) */
+  int64_t gumbel_row_stride;
+  const float* uniforms;       /* icdf: [B] in [0,1) */
+
+  /* special-token masking */
+  const uint8_t* suppress_mask; /* optional bool [V]: true -> logit = -1e9 */
+  int32_t eos_id;               /* EOS id for min-new-tokens gating (-1 = none) */
+  int32_t reserved0;
+
+  /* outputs */
+  int64_t* ids_i64;            /* [B] (either or both of ids_i64 / ids_i32) */
+  int32_t* ids_i32;
+  int64_t* counts_out;         /* optional [B, counts_out_row_stride]: token_counts +
+                                  one_hot(id); may equal token_counts (in-place +1) */
+  int64_t counts_out_row_stride;
+  float* processed_logits;     /* optional [B, processed_row_stride] fp32 (verification) */
+  int64_t processed_row_stride;
+  int32_t* row_flags;          /* optional [B], Q3S_ROW_* bits */
+  int32_t* error_word;         /* optional single device int32, Q3S_DEVERR_* bits */
+} q3s_sample_desc;
+
+/* Stage producer of the code-predictor frame. */
+typedef enum q3s_cp_producer {
+  Q3S_CP_DIRECT = 0,  /* stage j reads logits[j] as given */
+  Q3S_CP_ROTATE = 1   /* stage j reads logits[j][b][(v + id_{j-1}[b]) mod V], id_{-1} = ids_init */
+} q3s_cp_producer;
+
+/* All code-predictor stages of one frame for B rows, one persistent kernel. */
+typedef struct q3s_cp_frame_desc {
+  uint32_t struct_size;        /* = sizeof(q3s_cp_frame_desc) */
+  int32_t mode;                /* q3s_draw_mode */
+  int32_t batch;
+  int32_t vocab;
+  int32_t stages;              /* S, 1..Q3S_MAX_CP_STAGES (reference: 15) */
+  int32_t topk;                /* K (reference: min(50, V)) */
+  int32_t logits_dtype;
+  int32_t producer;            /* q3s_cp_producer */
+  const void* logits;          /* [S, B, V] with the strides below */
+  int64_t logits_row_stride;   /* elements */
+  int64_t logits_stage_stride; /* elements */
+  const int64_t* ids_init;     /* [B], ROTATE only */
+  const float* temperature;    float temperature_default;
+  const float* top_p;          float top_p_default;          /* icdf only */
+  const float* gumbel_noise;   /* gumbel: [B, S, >=K] (cp_gumbel_noise layout); NULL = greedy */
+  int64_t gumbel_row_stride;   /* elements between rows */
+  int64_t gumbel_stage_stride; /* elements between stages */
+  const float* uniforms;       /* icdf: [B, S] */
+  int64_t* ids_out;            /* [B, S] int64 (reference cp_tokens layout) */
+  int32_t* row_flags;          /* optional [B, S] */
+  int32_t* error_word;         /* optional */
+} q3s_cp_frame_desc;
+
+/* Sample one token per row.  Replaces talker_unified_modules.py:407-422,
+ * utils.py:1178-1193 and prefill_compare.py:383-399 (see above). */
+q3s_status q3s_sample(const q3s_sample_desc* desc, void* stream);
+
+/* Sample all stages of a code-predictor frame in one persistent launch.
+ * Replaces the sampling loop of utils.py:1218-1237. */
+q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* desc, void* stream);
+
+/* Message for the calling thread's most recent non-OK status ("" if none). */
+const char* q3s_last_error_string(void);
+
+/* Q3S_ABI_VERSION of the loaded library. */
+int32_t q3s_abi_version(void);
+
+/* sizeof() of the two descriptors as compiled into the library, so a binding
+ * can check its own struct layout (which: 0 = sample, 1 = cp_frame). */
+uint32_t q3s_desc_size(int32_t which);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q3S_SAMPLER_H */

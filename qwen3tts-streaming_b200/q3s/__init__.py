@@ -1,0 +1,35 @@
+"""q3s -- B200-native codec-token sampler for Qwen3TTS-Streaming's decode step.
+
+Python host side over the C ABI of ``include/q3s_sampler.h``; the sampling
+itself runs only in the sm_100a kernels of ``libq3s_sampler.so``.
+"""
+from . import _lib
+from .ops import (
+    CodecSampler,
+    CpFramePlan,
+    SamplePlan,
+    sample_codebook0,
+    sample_cp_frame,
+    sample_packed,
+    sample_token,
+    select_token,
+    suppress_mask,
+)
+
+__all__ = [
+    "CodecSampler",
+    "CpFramePlan",
+    "SamplePlan",
+    "sample_codebook0",
+    "sample_cp_frame",
+    "sample_packed",
+    "sample_token",
+    "select_token",
+    "suppress_mask",
+    "load_library",
+]
+
+
+def load_library():
+    """Load the CUDA library (raises if it has not been built)."""
+    return _lib.load()

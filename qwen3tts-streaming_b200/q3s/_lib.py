@@ -1,0 +1,155 @@
+"""ctypes binding of the C ABI in ``include/q3s_sampler.h``.
+
+The structures below mirror the C descriptors field for field; ``load()``
+checks their sizes against ``q3s_desc_size`` so a stale library or a layout
+drift fails at import instead of corrupting a launch.  There is no CPU
+fallback: if the library is missing, ``load()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+from .build import LIB_PATH
+
+Q3S_ABI_VERSION = 1
+MAX_VOCAB = 8192
+MAX_TOPK = 1024
+MAX_CP_STAGES = 64
+
+OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+DRAW_GUMBEL, DRAW_ICDF = 0, 1
+DTYPE_F32, DTYPE_BF16 = 0, 1
+CP_DIRECT, CP_ROTATE = 0, 1
+
+ROW_DRAW_BOUNDARY, ROW_TOPP_BOUNDARY, ROW_GREEDY, ROW_FALLBACK = 1, 2, 4, 8
+DEVERR_HISTORY_ID, DEVERR_OFFSETS, DEVERR_NO_MASS, DEVERR_WAIT_TIMEOUT, DEVERR_CANDIDATES = 1, 2, 4, 8, 16
+
+_p = C.c_void_p
+
+
+class SampleDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("mode", C.c_int32),
+        ("batch", C.c_int32),
+        ("vocab", C.c_int32),
+        ("topk", C.c_int32),
+        ("logits_dtype", C.c_int32),
+        ("logits_row_stride", C.c_int64),
+        ("logits", _p),
+        ("col_shift", _p),
+        ("token_counts", _p),
+        ("token_counts_row_stride", C.c_int64),
+        ("history", _p),
+        ("offsets", _p),
+        ("history_len", C.c_int64),
+        ("temperature", _p),
+        ("temperature_default", C.c_float),
+        ("top_k", _p),
+        ("top_p", _p),
+        ("top_p_default", C.c_float),
+        ("penalty", _p),
+        ("penalty_default", C.c_float),
+        ("min_new_tokens", _p),
+        ("min_new_tokens_default", C.c_int32),
+        ("cur_len", _p),
+        ("gumbel_noise", _p),
+        ("gumbel_row_stride", C.c_int64),
+        ("uniforms", _p),
+        ("suppress_mask", _p),
+        ("eos_id", C.c_int32),
+        ("reserved0", C.c_int32),
+        ("ids_i64", _p),
+        ("ids_i32", _p),
+        ("counts_out", _p),
+        ("counts_out_row_stride", C.c_int64),
+        ("processed_logits", _p),
+        ("processed_row_stride", C.c_int64),
+        ("row_flags", _p),
+        ("error_word", _p),
+    ]
+
+
+class CpFrameDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("mode", C.c_int32),
+        ("batch", C.c_int32),
+        ("vocab", C.c_int32),
+        ("stages", C.c_int32),
+        ("topk", C.c_int32),
+        ("logits_dtype", C.c_int32),
+        ("producer", C.c_int32),
+        ("logits", _p),
+        ("logits_row_stride", C.c_int64),
+        ("logits_stage_stride", C.c_int64),
+        ("ids_init", _p),
+        ("temperature", _p),
+        ("temperature_default", C.c_float),
+        ("top_p", _p),
+        ("top_p_default", C.c_float),
+        ("gumbel_noise", _p),
+        ("gumbel_row_stride", C.c_int64),
+        ("gumbel_stage_stride", C.c_int64),
+        ("uniforms", _p),
+        ("ids_out", _p),
+        ("row_flags", _p),
+        ("error_word", _p),
+    ]
+
+
+# every symbol include/q3s_sampler.h declares
+EXPORTS = (
+    "q3s_sample",
+    "q3s_sample_cp_frame",
+    "q3s_last_error_string",
+    "q3s_abi_version",
+    "q3s_desc_size",
+)
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: str | Path | None = None) -> C.CDLL:
+    """Load (once) and type the library.  Raises if it is missing or stale."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"q3s CUDA library not found at {p}; build it with __graft_entry__.build() "
+                "(there is no CPU fallback for the sampler)")
+        lib = C.CDLL(str(p))
+        lib.q3s_sample.argtypes = [C.POINTER(SampleDesc), _p]
+        lib.q3s_sample.restype = C.c_int
+        lib.q3s_sample_cp_frame.argtypes = [C.POINTER(CpFrameDesc), _p]
+        lib.q3s_sample_cp_frame.restype = C.c_int
+        lib.q3s_last_error_string.argtypes = []
+        lib.q3s_last_error_string.restype = C.c_char_p
+        lib.q3s_abi_version.argtypes = []
+        lib.q3s_abi_version.restype = C.c_int32
+        lib.q3s_desc_size.argtypes = [C.c_int32]
+        lib.q3s_desc_size.restype = C.c_uint32
+        if lib.q3s_abi_version() != Q3S_ABI_VERSION:
+            raise RuntimeError(f"q3s ABI {lib.q3s_abi_version()} != binding {Q3S_ABI_VERSION}; rebuild")
+        for which, st in ((0, SampleDesc), (1, CpFrameDesc)):
+            if lib.q3s_desc_size(which) != C.sizeof(st):
+                raise RuntimeError(f"q3s descriptor {st.__name__} size {C.sizeof(st)} != library "
+                                   f"{lib.q3s_desc_size(which)}; rebuild")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().q3s_last_error_string().decode("utf-8", "replace")
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        raise RuntimeError(f"{what} failed (status {status}): {last_error()}")

@@ -1,0 +1,352 @@
+"""CUDA kernels (through the C ABI) against the CPU oracle and the reference's
+golden vectors.
+
+Tolerances (stated by the benchmark contract):
+  * sampled ids bit-exact, except rows the oracle or the kernel flags as a
+    boundary draw (within 1e-6 of a CDF edge or of the top-p cut), which are
+    counted and bounded;
+  * processed logits within 1e-5 relative in fp32 (they are in fact compared
+    bit-exactly where both sides apply the same IEEE operations).
+"""
+import numpy as np
+import pytest
+import torch
+
+import q3s
+import q3s_oracle as O
+from conftest import load_golden
+from q3s import _lib, workloads
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+MAX_BOUNDARY_FRACTION = 0.02
+
+
+def _dev(x, dev):
+    return torch.as_tensor(np.ascontiguousarray(x)).to(dev)
+
+
+def _proc_close(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    same_inf = np.isinf(a) == np.isinf(b)
+    fin = np.isfinite(a) & np.isfinite(b)
+    return bool(np.all(same_inf) and np.all(a[np.isinf(a)] == b[np.isinf(a)])
+                and np.all(np.abs(a[fin] - b[fin]) <= RTOL * np.abs(b[fin]) + 1e-30))
+
+
+def run_icdf_batch(b: workloads.Batch, dev, *, processed=True):
+    g = b.to(dev)
+    B, V = g.B, g.V
+    proc = torch.empty(B, V, dtype=torch.float32, device=dev) if processed else None
+    flags = torch.zeros(B, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ids = q3s.sample_packed(g.logits, g.history, g.offsets, uniforms=g.uniforms, temperature=g.temperature,
+                            top_k=g.top_k, top_p=g.top_p, penalty=g.penalty, min_new_tokens=g.min_new_tokens,
+                            suppress=g.suppress, eos_id=g.eos_id, processed=proc, row_flags=flags,
+                            error_word=err)
+    torch.cuda.synchronize()
+    return (ids.cpu().numpy(), None if proc is None else proc.cpu().numpy(), flags.cpu().numpy(),
+            int(err.item()))
+
+
+def oracle_icdf(b: workloads.Batch):
+    return O.sample_icdf(b.logits, uniforms=b.uniforms.numpy(), temperature=b.temperature.numpy(),
+                         top_k=b.top_k.numpy(), top_p=b.top_p.numpy(), penalty=b.penalty.numpy(),
+                         history=b.history.numpy(), offsets=b.offsets.numpy(),
+                         min_new_tokens=b.min_new_tokens.numpy(), suppress=b.suppress.numpy(), eos_id=b.eos_id)
+
+
+def assert_ids_match(ids, ref, kflags, label):
+    bnd = ref["boundary"] | ((kflags & (_lib.ROW_DRAW_BOUNDARY | _lib.ROW_TOPP_BOUNDARY)) != 0)
+    bad = (ids != ref["ids"]) & ~bnd
+    assert not bad.any(), f"{label}: {bad.sum()} non-boundary mismatches at rows {np.nonzero(bad)[0][:10]}"
+    assert bnd.mean() <= MAX_BOUNDARY_FRACTION + 1.0 / len(ids), f"{label}: {bnd.sum()} boundary rows"
+    return int(bnd.sum()), int(((ids != ref["ids"]) & bnd).sum())
+
+
+# ---------------------------------------------------------------------------
+# golden vectors from the reference
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name", ["gumbel_cb0_f32", "gumbel_cb0_bf16"])
+@pytest.mark.parametrize("inplace", [False, True])
+def test_codebook0_gumbel_matches_reference_golden(cuda_device, q3s_lib, name, inplace):
+    g = load_golden(name)
+    B, V = g["logits"].shape
+    tc = np.zeros((B, V), np.int64)
+    for b in range(B):
+        np.add.at(tc[b], g["history"][g["offsets"][b]:g["offsets"][b + 1]], 1)
+    logits = g["logits_bf16"].to(cuda_device) if "logits_bf16" in g else _dev(g["logits"], cuda_device)
+    tcd = _dev(tc, cuda_device)
+    sampler = q3s.CodecSampler(device=cuda_device)
+    ids, upd = sampler.codebook0(logits, tcd, _dev(g["gumbel_noise"], cuda_device),
+                                 _dev(g["temperature"].reshape(B, 1), cuda_device),
+                                 _dev(g["penalty"].reshape(B, 1), cuda_device), inplace=inplace)
+    ids = ids.cpu().numpy()
+    ok = ~g["tie_rows"]
+    np.testing.assert_array_equal(ids[ok], g["ids"][ok])
+    oracle = O.sample_gumbel(g["logits"], gumbel_noise=g["gumbel_noise"], temperature=g["temperature"],
+                             penalty=g["penalty"], token_counts=tc, suppress=O.suppress_mask(V), topk=50)
+    np.testing.assert_array_equal(ids, oracle["ids"])  # canonical tie rule on every row
+    np.testing.assert_array_equal(upd.cpu().numpy(), oracle["updated_counts"])
+    if inplace:
+        assert upd.data_ptr() == tcd.data_ptr()
+
+
+def test_cp_select_matches_reference_golden(cuda_device, q3s_lib):
+    g = load_golden("cp_select")
+    B = g["logits"].shape[0]
+    lg = _dev(g["logits"], cuda_device).reshape(B, 1, -1)
+    ids = q3s.select_token(lg, temperature=_dev(g["temperature"].reshape(B, 1), cuda_device),
+                           gumbel_noise=_dev(g["gumbel_noise"], cuda_device))
+    np.testing.assert_array_equal(ids.cpu().numpy(), g["ids"])
+    np.testing.assert_array_equal(q3s.select_token(lg).cpu().numpy(), g["greedy_ids"])
+
+
+def test_icdf_matches_reference_sample_token_golden(cuda_device, q3s_lib):
+    g = load_golden("icdf_sample_token")
+    B, V = g["logits"].shape
+    ref = O.sample_icdf(g["logits"], uniforms=g["uniforms"], temperature=g["temperature"], top_k=g["top_k"],
+                        penalty=g["penalty"], history=g["history"], offsets=g["offsets"],
+                        suppress=O.suppress_mask(V), eos_id=2150)
+    proc = torch.empty(B, V, dtype=torch.float32, device=cuda_device)
+    flags = torch.zeros(B, dtype=torch.int32, device=cuda_device)
+    ids = q3s.sample_packed(g["logits_bf16"].to(cuda_device), _dev(g["history"], cuda_device),
+                            _dev(g["offsets"], cuda_device), uniforms=_dev(g["uniforms"], cuda_device),
+                            temperature=_dev(g["temperature"], cuda_device), top_k=_dev(g["top_k"], cuda_device),
+                            top_p=1.0, penalty=_dev(g["penalty"], cuda_device), min_new_tokens=0,
+                            suppress=q3s.suppress_mask(V, 2150, cuda_device), processed=proc, row_flags=flags)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(proc.cpu().numpy(), g["processed"])  # bit-exact
+    assert_ids_match(ids.cpu().numpy(), {"ids": g["ids"], "boundary": ref["boundary"]}, flags.cpu().numpy(),
+                     "sample_token golden")
+
+
+def test_icdf_matches_hf_extended_golden(cuda_device, q3s_lib):
+    g = load_golden("icdf_hf_extended")
+    B, V = g["logits"].shape
+    ref = O.sample_icdf(g["logits"], uniforms=g["uniforms"], temperature=g["temperature"], top_k=g["top_k"],
+                        top_p=g["top_p"], penalty=g["penalty"], history=g["history"], offsets=g["offsets"],
+                        min_new_tokens=g["min_new_tokens"], suppress=O.suppress_mask(V), eos_id=2150)
+    proc = torch.empty(B, V, dtype=torch.float32, device=cuda_device)
+    flags = torch.zeros(B, dtype=torch.int32, device=cuda_device)
+    ids = q3s.sample_packed(g["logits_bf16"].to(cuda_device), _dev(g["history"], cuda_device),
+                            _dev(g["offsets"], cuda_device), uniforms=_dev(g["uniforms"], cuda_device),
+                            temperature=_dev(g["temperature"], cuda_device), top_k=_dev(g["top_k"], cuda_device),
+                            top_p=_dev(g["top_p"], cuda_device), penalty=_dev(g["penalty"], cuda_device),
+                            min_new_tokens=_dev(g["min_new_tokens"], cuda_device),
+                            suppress=q3s.suppress_mask(V, 2150, cuda_device), processed=proc, row_flags=flags)
+    torch.cuda.synchronize()
+    kf = flags.cpu().numpy()
+    ok = ~(ref["boundary"] | ((kf & 3) != 0))
+    assert _proc_close(proc.cpu().numpy()[ok], g["processed"][ok])
+    assert_ids_match(ids.cpu().numpy(), {"ids": g["ids"], "boundary": ~ok}, kf, "hf extended golden")
+
+
+# ---------------------------------------------------------------------------
+# benchmark configurations against the oracle
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("cfg,rows", [(0, None), (1, None), (3, None), (4, None)])
+def test_configs_match_oracle(cuda_device, q3s_lib, cfg, rows):
+    b = workloads.make_batch(cfg, rows=rows)
+    ids, proc, kf, err = run_icdf_batch(b, cuda_device)
+    ref = oracle_icdf(b)
+    assert err == 0
+    nb, nbm = assert_ids_match(ids, ref, kf, f"config {cfg}")
+    ok = ~(ref["boundary"] | ((kf & 3) != 0))
+    assert _proc_close(proc[ok], ref["processed"][ok])
+    greedy = b.temperature.numpy() <= 0
+    assert np.all((kf[greedy] & _lib.ROW_GREEDY) != 0)
+    print(f"config {cfg}: {len(ids)} rows, {nb} boundary rows, {nbm} of them differ")
+
+
+def test_gumbel_packed_matches_oracle(cuda_device, q3s_lib):
+    b = workloads.make_batch(1)
+    g = b.to(cuda_device)
+    ids = q3s.sample_packed(g.logits, g.history, g.offsets, mode="gumbel", topk=50, gumbel_noise=g.gumbel_noise,
+                            temperature=g.temperature, penalty=g.penalty, suppress=g.suppress, eos_id=b.eos_id,
+                            min_new_tokens=g.min_new_tokens)
+    ref = O.sample_gumbel(b.logits, gumbel_noise=b.gumbel_noise.numpy(), temperature=b.temperature.numpy(),
+                          penalty=b.penalty.numpy(), history=b.history.numpy(), offsets=b.offsets.numpy(),
+                          suppress=b.suppress.numpy(), topk=50, eos_id=b.eos_id,
+                          min_new_tokens=b.min_new_tokens.numpy())
+    np.testing.assert_array_equal(ids.cpu().numpy(), ref["ids"])
+
+
+def test_deterministic_across_runs(cuda_device, q3s_lib):
+    b = workloads.make_batch(4, rows=(0, 256))
+    a1, p1, f1, _ = run_icdf_batch(b, cuda_device)
+    a2, p2, f2, _ = run_icdf_batch(b, cuda_device)
+    np.testing.assert_array_equal(a1, a2)
+    np.testing.assert_array_equal(p1.view(np.uint32), p2.view(np.uint32))
+    np.testing.assert_array_equal(f1, f2)
+
+
+# ---------------------------------------------------------------------------
+# edge cases
+# ---------------------------------------------------------------------------
+
+def _icdf_case(dev, logits, *, T=1.0, k=0, p=1.0, pen=1.0, hist=None, u=None, mn=0, eos=-1, suppress=None):
+    logits = np.asarray(logits, np.float32)
+    B, V = logits.shape
+    rng = np.random.default_rng(0)
+    u = rng.random(B).astype(np.float32) if u is None else np.asarray(u, np.float32)
+    if hist is None:
+        hist = [np.zeros(0, np.int32)] * B
+    offs = np.zeros(B + 1, np.int32)
+    offs[1:] = np.cumsum([len(h) for h in hist])
+    flat = np.concatenate(hist).astype(np.int32) if offs[-1] else np.zeros(1, np.int32)
+    ref = O.sample_icdf(logits, uniforms=u, temperature=np.full(B, T, np.float32), top_k=np.full(B, k),
+                        top_p=np.full(B, p, np.float32), penalty=np.full(B, pen, np.float32),
+                        history=flat[:offs[-1]], offsets=offs, min_new_tokens=np.full(B, mn),
+                        suppress=suppress, eos_id=eos)
+    proc = torch.empty(B, V, dtype=torch.float32, device=dev)
+    flags = torch.zeros(B, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ids = q3s.sample_packed(_dev(logits, dev), _dev(flat, dev), _dev(offs, dev), uniforms=_dev(u, dev),
+                            temperature=T, top_k=k, top_p=p, penalty=pen, min_new_tokens=mn, eos_id=eos,
+                            suppress=None if suppress is None else _dev(suppress, dev), processed=proc,
+                            row_flags=flags, error_word=err)
+    torch.cuda.synchronize()
+    return ids.cpu().numpy(), proc.cpu().numpy(), flags.cpu().numpy(), int(err.item()), ref
+
+
+@pytest.mark.parametrize("V", [1, 7, 64, 1000, 2048, 3072, 4100, 8192])
+@pytest.mark.parametrize("k,p", [(0, 1.0), (50, 1.0), (50, 0.9), (0, 0.95), (1, 1.0)])
+def test_vocab_sizes_and_filters(cuda_device, q3s_lib, V, k, p):
+    rng = np.random.default_rng(V * 7 + k)
+    x = (rng.standard_normal((6, V)) * 2.0).astype(np.float32)
+    ids, proc, kf, err, ref = _icdf_case(cuda_device, x, T=0.8, k=k, p=p)
+    assert err == 0
+    assert_ids_match(ids, ref, kf, f"V={V} k={k} p={p}")
+    ok = ~(ref["boundary"] | ((kf & 3) != 0))
+    assert _proc_close(proc[ok], ref["processed"][ok])
+
+
+def test_heavy_ties_and_top_k_boundary_ties(cuda_device, q3s_lib):
+    x = np.zeros((4, 512), np.float32)
+    x[:, :100] = 1.0           # 100-way tie across the k=50 boundary: HF keeps all of them
+    x[1] = 0.0                 # a fully flat row
+    x[2, ::3] = -np.inf
+    ids, proc, kf, err, ref = _icdf_case(cuda_device, x, k=50, p=0.7)
+    assert_ids_match(ids, ref, kf, "ties")
+    ok = ~(ref["boundary"] | ((kf & 3) != 0))
+    assert _proc_close(proc[ok], ref["processed"][ok])
+
+
+def test_extreme_uniforms_and_tiny_top_p(cuda_device, q3s_lib):
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((6, 3072)) * 3).astype(np.float32)
+    u = np.array([0.0, 0.0, np.float32(1 - 2**-24), np.float32(1 - 2**-24), 0.5, 0.25], np.float32)
+    ids, _, kf, _, ref = _icdf_case(cuda_device, x, k=0, p=1e-4, u=u)
+    np.testing.assert_array_equal(ids, x.argmax(-1))  # top-p this small keeps only the top entry
+    ids, _, kf, _, ref = _icdf_case(cuda_device, x, k=100, p=1.0, u=u)
+    assert_ids_match(ids, ref, kf, "extreme uniforms")
+
+
+def test_penalty_eos_gate_and_suppress(cuda_device, q3s_lib):
+    rng = np.random.default_rng(4)
+    x = (rng.standard_normal((8, 3072)) * 3).astype(np.float32)
+    x[:, 2150] = 50.0  # EOS would win everywhere unless gated
+    hist = [rng.integers(0, 3072, n).astype(np.int32) for n in (0, 1, 5, 9, 30, 64, 65, 200)]
+    sup = O.suppress_mask(3072, 2150)
+    ids, proc, kf, err, ref = _icdf_case(cuda_device, x, T=0.9, k=50, p=0.9, pen=1.3, hist=hist, mn=64,
+                                         eos=2150, suppress=sup)
+    assert err == 0
+    assert_ids_match(ids, ref, kf, "penalty/eos")
+    lens = np.array([len(h) for h in hist])
+    assert np.all(ids[lens < 64] != 2150) and np.all(ids[lens >= 64] == 2150)
+    ok = ~(ref["boundary"] | ((kf & 3) != 0))
+    assert _proc_close(proc[ok], ref["processed"][ok])
+
+
+def test_bad_history_is_reported_not_faulted(cuda_device, q3s_lib):
+    x = np.zeros((2, 256), np.float32)
+    hist = [np.array([5, 300, -1], np.int32), np.array([7], np.int32)]
+    ids, _, _, err, _ = _icdf_case(cuda_device, x, hist=hist)
+    assert err & _lib.DEVERR_HISTORY_ID
+    dev = cuda_device
+    err_t = torch.zeros(1, dtype=torch.int32, device=dev)
+    bad_offs = torch.tensor([0, 5, 2], dtype=torch.int32, device=dev)  # non-monotone
+    q3s.sample_packed(torch.zeros(2, 256, device=dev), torch.zeros(5, dtype=torch.int32, device=dev), bad_offs,
+                      uniforms=torch.zeros(2, device=dev), error_word=err_t)
+    torch.cuda.synchronize()
+    assert int(err_t.item()) & _lib.DEVERR_OFFSETS
+
+
+def test_strided_and_3d_logits(cuda_device, q3s_lib):
+    dev = cuda_device
+    rng = np.random.default_rng(5)
+    full = (rng.standard_normal((4, 3, 3072)) * 3).astype(np.float32)
+    noise = rng.gumbel(size=(4, 50)).astype(np.float32)
+    tc = np.zeros((4, 3072), np.int64)
+    ids, _ = q3s.sample_codebook0(_dev(full, dev), _dev(tc, dev), _dev(noise, dev), 0.9, 1.05)
+    ref = O.sample_gumbel(full[:, -1, :], gumbel_noise=noise, temperature=np.full(4, 0.9, np.float32),
+                          penalty=np.full(4, 1.05, np.float32), token_counts=tc, topk=50)
+    np.testing.assert_array_equal(ids.cpu().numpy(), ref["ids"])
+
+
+def test_col_shift_reads_rotated_rows(cuda_device, q3s_lib):
+    dev = cuda_device
+    rng = np.random.default_rng(6)
+    base = torch.from_numpy((rng.standard_normal((16, 2048)) * 2.5).astype(np.float32)).to(torch.bfloat16)
+    shift = rng.integers(0, 2048, 16)
+    noise = rng.gumbel(size=(16, 50)).astype(np.float32)
+    plan = q3s.SamplePlan(base.to(dev), mode="gumbel", topk=50, temperature=0.9,
+                          gumbel_noise=_dev(noise, dev), col_shift=_dev(shift, dev))
+    plan.launch()
+    ref = O.select_token_cp(O.rotate_rows(base.float().numpy(), shift), temperature=np.full(16, 0.9, np.float32),
+                            gumbel_noise=noise, topk=50)
+    np.testing.assert_array_equal(plan.ids.cpu().numpy(), ref)
+
+
+# ---------------------------------------------------------------------------
+# code-predictor frame
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("mode", ["gumbel", "icdf", "greedy"])
+@pytest.mark.parametrize("rotate", [True, False])
+def test_cp_frame_matches_oracle_chain(cuda_device, q3s_lib, mode, rotate):
+    f = workloads.make_cp_frame()
+    g = f.to(cuda_device)
+    flags = torch.zeros(f.B, f.S, dtype=torch.int32, device=cuda_device)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ids = q3s.sample_cp_frame(g.base, mode="icdf" if mode == "icdf" else "gumbel", ids_init=g.ids_init,
+                              rotate=rotate, temperature=g.temperature, topk=50, top_p=1.0,
+                              gumbel_noise=g.gumbel_noise if mode == "gumbel" else None,
+                              uniforms=g.uniforms, row_flags=flags, error_word=err).cpu().numpy()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = O.cp_frame(f.base.float().numpy(), mode="icdf" if mode == "icdf" else "gumbel",
+                     ids_init=f.ids_init.numpy(), rotate=rotate, temperature=f.temperature.numpy(), topk=50,
+                     gumbel_noise=f.gumbel_noise.numpy() if mode == "gumbel" else None,
+                     uniforms=f.uniforms.numpy())
+    if mode == "icdf":
+        # a boundary draw in stage j legitimately changes every later stage of that row
+        kf = flags.cpu().numpy()
+        bnd = ref["boundary"] | ((kf & 3) != 0)
+        first_bnd = np.where(bnd.any(1), bnd.argmax(1), f.S)
+        for b in range(f.B):
+            np.testing.assert_array_equal(ids[b, :first_bnd[b]], ref["ids"][b, :first_bnd[b]])
+        assert (first_bnd < f.S).mean() < 0.1
+    else:
+        np.testing.assert_array_equal(ids, ref["ids"])
+
+
+def test_cp_frame_equals_fifteen_single_stage_launches(cuda_device, q3s_lib):
+    f = workloads.make_cp_frame()
+    g = f.to(cuda_device)
+    frame = q3s.sample_cp_frame(g.base, mode="gumbel", ids_init=g.ids_init, rotate=True,
+                                temperature=g.temperature, topk=50, gumbel_noise=g.gumbel_noise)
+    prev = g.ids_init.clone()
+    outs = []
+    for j in range(f.S):
+        plan = q3s.SamplePlan(g.base[j], mode="gumbel", topk=50, temperature=g.temperature,
+                              gumbel_noise=g.gumbel_noise[:, j, :], col_shift=prev)
+        plan.launch()
+        prev = plan.ids
+        outs.append(prev)
+    np.testing.assert_array_equal(torch.stack(outs, 1).cpu().numpy(), frame.cpu().numpy())
