@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--no-extra", action="store_true", help="skip the per-config extra measurements")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bound on the CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--profile-config", type=int, default=None,
+                    help="plain eager launches of one config (0-4; 2 = code-predictor frame) for ncu; "
+                         "prints no bench value")
     return ap.parse_args()
 
 
@@ -526,8 +529,37 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(args):
+    """W + K eager launches of one configuration over 4 input copies (ncu target)."""
+    import torch
+
+    import q3s
+    from q3s import workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    q3s.load_library()
+    cfg = args.profile_config
+    if cfg == 2:
+        f = workloads.make_cp_frame().to(dev)
+        plans = [q3s.CpFramePlan(f.base if i == 0 else f.base.clone(), mode="gumbel", topk=50,
+                                 ids_init=f.ids_init, rotate=True, temperature=f.temperature,
+                                 gumbel_noise=f.gumbel_noise) for i in range(4)]
+    else:
+        b = workloads.make_batch(cfg).to(dev)
+        plans = plans_for([b] + [clone_batch(b) for _ in range(3)])
+    n = max(3, args.warmup) + max(1, args.steps)
+    for i in range(n):
+        plans[i % len(plans)].launch()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": True, "config": cfg, "launches": n}), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.profile_config is not None:
+        run_profile(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

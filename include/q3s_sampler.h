@@ -51,7 +51,7 @@ extern "C" {
 
 #define Q3S_ABI_VERSION 1
 #define Q3S_MAX_VOCAB 8192     /* one CTA holds a whole row on chip */
-#define Q3S_MAX_TOPK 1024      /* largest exactly-K candidate set (gumbel mode) */
+#define Q3S_MAX_TOPK 512       /* largest exactly-K candidate set (gumbel mode) */
 #define Q3S_MAX_CP_STAGES 64
 
 typedef enum q3s_status {

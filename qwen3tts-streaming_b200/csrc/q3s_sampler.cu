@@ -68,6 +68,7 @@ struct SampleArgs {
   bool vec_logits;
   bool vec_counts;
   bool vec_suppress;
+  bool vec_history;
 };
 
 struct CpArgs {
@@ -96,31 +97,38 @@ constexpr int MAX_NBUF = 8;
 // loads
 // ---------------------------------------------------------------------------
 
-// The 8 logits of vocabulary entries [v0, v0+8) of one row, fp32.  `shift`
+// The E logits of vocabulary entries [v0, v0+E) of one row, as fp32.  `shift`
 // (in [0,V)) reads column v at (v + shift) mod V.  Entries >= V are -inf and
 // cleared from `vmask`.
-template <bool BF16>
-Q3S_DEV void load_logits8(const void* base, int64_t row_off, int V, int v0, int shift,
-                          bool vec, float (&x)[E], uint32_t& vmask) {
+template <bool BF16, int E>
+Q3S_DEV void load_logits(const void* base, int64_t row_off, int V, int v0, int shift, bool vec, float (&x)[E],
+                         uint32_t& vmask) {
   vmask = 0;
   if (shift == 0 && vec && v0 + E <= V) {
     if (BF16) {
-      const uint4 r = ld_stream16(static_cast<const uint16_t*>(base) + row_off + v0);
-      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+      const uint16_t* p = static_cast<const uint16_t*>(base) + row_off + v0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        x[2 * i] = bf16_bits_to_f32(w[i] & 0xffffu);
-        x[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16);
+      for (int c = 0; c < E / 8; ++c) {
+        const uint4 r = ld_stream16(p + 8 * c);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[8 * c + 2 * i] = bf16_bits_to_f32(w[i] & 0xffffu);
+          x[8 * c + 2 * i + 1] = bf16_bits_to_f32(w[i] >> 16);
+        }
       }
     } else {
       const float* p = static_cast<const float*>(base) + row_off + v0;
-      const uint4 r0 = ld_stream16(p), r1 = ld_stream16(p + 4);
-      x[0] = __uint_as_float(r0.x); x[1] = __uint_as_float(r0.y);
-      x[2] = __uint_as_float(r0.z); x[3] = __uint_as_float(r0.w);
-      x[4] = __uint_as_float(r1.x); x[5] = __uint_as_float(r1.y);
-      x[6] = __uint_as_float(r1.z); x[7] = __uint_as_float(r1.w);
+#pragma unroll
+      for (int c = 0; c < E / 4; ++c) {
+        const uint4 r = ld_stream16(p + 4 * c);
+        x[4 * c] = __uint_as_float(r.x);
+        x[4 * c + 1] = __uint_as_float(r.y);
+        x[4 * c + 2] = __uint_as_float(r.z);
+        x[4 * c + 3] = __uint_as_float(r.w);
+      }
     }
-    vmask = 0xffu;
+    vmask = (E == 32) ? 0xffffffffu : ((1u << E) - 1u);
     return;
   }
 #pragma unroll
@@ -137,6 +145,22 @@ Q3S_DEV void load_logits8(const void* base, int64_t row_off, int V, int v0, int 
       vmask |= 1u << j;
     }
   }
+}
+
+// E byte flags (nonzero = set), 8-byte aligned -> bitmask.
+template <int E>
+Q3S_DEV uint32_t bytes_to_mask(const uint8_t* p) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int c = 0; c < E / 8; ++c) {
+    const uint2 f = *reinterpret_cast<const uint2*>(p + 8 * c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m |= (((f.x >> (8 * j)) & 0xffu) ? 1u : 0u) << (8 * c + j);
+      m |= (((f.y >> (8 * j)) & 0xffu) ? 1u : 0u) << (8 * c + j + 4);
+    }
+  }
+  return m;
 }
 
 Q3S_DEV int norm_shift(int64_t s, int V) {
@@ -159,42 +183,55 @@ struct RowCfg {
   const float* noise;  // gumbel noise of this row, indexed by rank
 };
 
-// Samples one id from the processed logits x (post suppress/penalty/EOS gate).
-// Every thread returns the same id and flags.  `processed` (optional) receives
-// the row handed to the draw: g0 (gumbel), the filtered s (icdf), x (greedy).
-template <int NT>
-Q3S_DEV int sample_core(const float (&x)[E], uint32_t vmask, int V, const RowCfg& c,
-                        Scratch<NT>& sh, float* processed, int& flags, uint32_t& err) {
+// Exact path: samples one id from the processed logits v (post suppress /
+// penalty / EOS gate, every entry exact; v is overwritten).  Used for rows
+// that keep the whole vocabulary and as the fallback of sample_core.  Every
+// thread returns the same id; `flags` is complete in the thread that owns the
+// id (v0 <= id < v0+E).  `processed` (optional) receives the row handed to
+// the draw: g0 (gumbel), the filtered s (icdf), x (greedy).  Needs sh.hist
+// all-zero on entry and leaves it so.
+template <int NT, int E, int MODE>
+Q3S_DEV int sample_exact(float (&v)[E], uint32_t vmask, int V, const RowCfg& c, Scratch<NT, E>& sh,
+                         float* processed, int& flags, uint32_t& err) {
   const int t = threadIdx.x;
   const int v0 = t * E;
+  int rb = 0;
   flags = 0;
+  if (t == 0) sh.flags = 0;  // published by the first barrier below
 
   if (c.greedy) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < E; ++j)
-      if (((vmask >> j) & 1u) && arg_better(x[j], v0 + j, bv, bi)) {
-        bv = x[j];
+      if (((vmask >> j) & 1u) && arg_better(v[j], v0 + j, bv, bi)) {
+        bv = v[j];
         bi = v0 + j;
       }
     if (processed) {
 #pragma unroll
       for (int j = 0; j < E; ++j)
-        if ((vmask >> j) & 1u) processed[v0 + j] = x[j];
+        if ((vmask >> j) & 1u) processed[v0 + j] = v[j];
     }
     flags = Q3S_ROW_GREEDY;
-    return block_argmax<NT>(bv, bi, bi, sh);
+    return block_argmax<NT, E>(bv, bi, bi, sh, rb);
   }
 
-  if (c.mode == Q3S_DRAW_GUMBEL) {
+  if (MODE == Q3S_DRAW_GUMBEL) {
     // talker_unified_modules.py:415-420 / utils.py:1189-1193
     const int K = c.k;
-    for (int r = t; r < K; r += NT) sh.cand_w[r] = __ldg(c.noise + r);
+    const int K4 = (K + 3) & ~3;
+    for (int r = t; r < K; r += NT) sh.noise[r] = __ldg(c.noise + r);
+    for (int r = K + t; r < K4; r += NT) sh.cand[r] = make_uint4(0u, 0x7fffffffu, 0u, 0u);  // never outranks
+    if (processed) {
+#pragma unroll
+      for (int j = 0; j < E; ++j)
+        if ((vmask >> j) & 1u) processed[v0 + j] = v[j];
+    }
     uint32_t key[E];
 #pragma unroll
-    for (int j = 0; j < E; ++j) key[j] = f2key(x[j]);
-    const uint32_t kth = select_kth_largest<NT>(key, vmask, K, sh);
+    for (int j = 0; j < E; ++j) key[j] = f2key(v[j]);
+    const uint32_t kth = select_kth_largest<NT, E>(key, vmask, K, sh, rb);
     uint32_t cg = 0, ce = 0;
 #pragma unroll
     for (int j = 0; j < E; ++j)
@@ -203,7 +240,7 @@ Q3S_DEV int sample_core(const float (&x)[E], uint32_t vmask, int V, const RowCfg
         ce += key[j] == kth;
       }
     uint32_t tot;
-    const uint32_t ex = block_excl_scan_u<NT>((cg << 16) | ce, tot, sh);
+    const uint32_t ex = block_excl_scan_u<NT, E>((cg << 16) | ce, tot, sh, rb);
     const uint32_t gt_tot = tot >> 16;
     const uint32_t need = static_cast<uint32_t>(K) - gt_tot;  // ties admitted, lowest index first
     uint32_t pg = ex >> 16, pe = ex & 0xffffu;
@@ -221,163 +258,249 @@ Q3S_DEV int sample_core(const float (&x)[E], uint32_t vmask, int V, const RowCfg
         err |= Q3S_DEVERR_CANDIDATES;
         slot = -1;
       }
-      if (slot >= 0) {
-        sh.cand_k[slot] = key[j];
-        sh.cand_v[slot] = x[j];
-        sh.cand_i[slot] = v0 + j;
-      }
+      if (slot >= 0) sh.cand[slot] = make_uint4(key[j], static_cast<uint32_t>(v0 + j), __float_as_uint(v[j]), 0u);
     }
     __syncthreads();
     float bs = -INFINITY;
     int br = 0x7fffffff, bid = 0x7fffffff;
     for (int ci = t; ci < K; ci += NT) {
-      const uint32_t kc = sh.cand_k[ci];
-      const int ic = sh.cand_i[ci];
+      const uint4 me = sh.cand[ci];
+      const int ic = static_cast<int>(me.y);
       int rank = 0;
-      for (int o = 0; o < K; ++o) {
-        const uint32_t ko = sh.cand_k[o];
-        rank += (ko > kc) || (ko == kc && sh.cand_i[o] < ic);
+      for (int o = 0; o < K4; o += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint4 ot = sh.cand[o + u];
+          rank += (ot.x > me.x) | ((ot.x == me.x) & (static_cast<int>(ot.y) < ic));
+        }
       }
-      const float score = __fadd_rn(__fdiv_rn(sh.cand_v[ci], c.T), sh.cand_w[rank]);
+      const float score = __fadd_rn(__fdiv_rn(__uint_as_float(me.z), c.T), sh.noise[rank]);
       if (arg_better(score, rank, bs, br)) {
         bs = score;
         br = rank;
         bid = ic;
       }
     }
-    if (processed) {
-#pragma unroll
-      for (int j = 0; j < E; ++j)
-        if ((vmask >> j) & 1u) processed[v0 + j] = x[j];
-    }
-    return block_argmax<NT>(bs, br, bid, sh);
+    return block_argmax<NT, E>(bs, br, bid, sh, rb);
   }
 
   // ---- icdf: Temperature -> TopK -> TopP -> softmax -> inverse CDF ----------
-  float s[E];
   uint32_t key[E];
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    s[j] = ((vmask >> j) & 1u) ? __fdiv_rn(x[j], c.T) : -INFINITY;
-    key[j] = f2key(s[j]);
-  }
   uint32_t smask = vmask;
   if (c.k > 0 && c.k < V) {
-    // HF TopKLogitsWarper: drop s < (k-th largest value); ties at it survive.
-    const uint32_t kth = select_kth_largest<NT>(key, vmask, c.k, sh);
+    // HF TopKLogitsWarper keeps s >= (k-th largest s), s = x / T.  Division
+    // by T > 0 is monotone, so the k-th largest s is RN(x_k / T) with x_k the
+    // k-th largest x, and the survivors are {x >= x_k} plus entries just below
+    // x_k whose quotient rounds onto it.  While quotients stay normal, one
+    // quotient's preimage spans < 2.0001 ulps of x, so only the 4 floats below
+    // x_k are divided to check; otherwise every entry is divided.
+#pragma unroll
+    for (int j = 0; j < E; ++j) key[j] = f2key(v[j]);
+    const uint32_t kx = select_kth_largest<NT, E>(key, vmask, c.k, sh, rb);
+    const float sk = __fdiv_rn(key2f(kx), c.T);
+    const float ask = fabsf(sk);
+    const bool window = ask >= 0x1p-100f && ask <= 0x1p100f && c.T >= 0x1p-20f && c.T <= 0x1p20f;
     smask = 0;
 #pragma unroll
+    for (int j = 0; j < E; ++j) {
+      if (!((vmask >> j) & 1u)) continue;
+      if (key[j] >= kx) {
+        v[j] = __fdiv_rn(v[j], c.T);
+        smask |= 1u << j;
+      } else if (!window || kx - key[j] <= 4u) {
+        const float sj = __fdiv_rn(v[j], c.T);
+        if (sj == sk) {
+          v[j] = sj;
+          smask |= 1u << j;
+        }
+      }
+    }
+  } else if (c.T != 1.0f) {  // x / 1 == x exactly
+#pragma unroll
     for (int j = 0; j < E; ++j)
-      if (((vmask >> j) & 1u) && key[j] >= kth) smask |= 1u << j;
+      if ((vmask >> j) & 1u) v[j] = __fdiv_rn(v[j], c.T);
   }
   float lm = -INFINITY;
 #pragma unroll
   for (int j = 0; j < E; ++j)
-    if ((smask >> j) & 1u) lm = fmaxf(lm, s[j]);
-  const float m = block_max_f<NT>(lm, sh);
+    if ((smask >> j) & 1u) lm = fmaxf(lm, v[j]);
+  uint32_t n;
+  float m;
+  const uint32_t pos0 = block_scan_count_max<NT, E>(__popc(smask), lm, n, m, sh, rb);
   if (m == -INFINITY) {
-    // nothing finite survived: report and fall back to the lowest index
+    // nothing finite survived: report and take the lowest index
     err |= Q3S_DEVERR_NO_MASS;
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < E; ++j)
-      if (((vmask >> j) & 1u) && arg_better(x[j], v0 + j, bv, bi)) {
-        bv = x[j];
-        bi = v0 + j;
-      }
     flags = Q3S_ROW_FALLBACK;
-    return block_argmax<NT>(bv, bi, bi, sh);
+    int first = 0x7fffffff;
+#pragma unroll
+    for (int j = E - 1; j >= 0; --j)
+      if ((vmask >> j) & 1u) first = v0 + j;
+    return block_min_i<NT, E>(first, sh, rb);
   }
 
+  if (n <= static_cast<uint32_t>(FINISH < NT ? FINISH : NT)) {
+    // ---- few survivors (every top-k row): finish on a compact list --------
+    // Candidate records in vocabulary order; top-p by all-pairs masses (one
+    // candidate per thread); the draw runs in warp 0 alone.
+    const int n4 = (static_cast<int>(n) + 3) & ~3;
+    uint32_t pos = pos0;
+#pragma unroll
+    for (int j = 0; j < E; ++j)
+      if ((smask >> j) & 1u) {
+        sh.cand[pos] = make_uint4(f2key(v[j]), static_cast<uint32_t>(v0 + j),
+                                  __float_as_uint(softmax_weight(v[j], m)), 0u);
+        ++pos;
+      }
+    if (t >= static_cast<int>(n) && t < n4) sh.cand[t] = make_uint4(0u, 0x7fffffffu, 0u, 0u);  // weightless
+    if (t < n4) sh.keep[t] = 1;
+    __syncthreads();
+    if (c.top_p < 1.0f) {
+      // HF TopPLogitsWarper over a stable ascending order (value asc, index
+      // asc): remove an entry when the softmax mass at-or-below it is <= 1-p;
+      // the ascending-last entry always stays.
+      const float frac = __fsub_rn(1.0f, c.top_p);
+      if (t < static_cast<int>(n)) {
+        const uint4 me = sh.cand[t];
+        const int ic = static_cast<int>(me.y);
+        float cum = 0.0f, Z = 0.0f;
+        int after = 0;
+        for (int o = 0; o < n4; o += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint4 ot = sh.cand[o + u];
+            const float w = __uint_as_float(ot.z);
+            const bool before = (ot.x < me.x) | ((ot.x == me.x) & (static_cast<int>(ot.y) <= ic));
+            cum = __fadd_rn(cum, before ? w : 0.0f);
+            Z = __fadd_rn(Z, w);
+            after += (!before) & (static_cast<int>(ot.y) != 0x7fffffff);
+          }
+        }
+        const float thr = __fmul_rn(frac, Z);
+        sh.keep[t] = (after == 0) || !(cum <= thr);
+        if (after != 0 && fabsf(__fsub_rn(cum, thr)) < BOUNDARY_EPS * Z) atomicOr(&sh.flags, Q3S_ROW_TOPP_BOUNDARY);
+      }
+      __syncthreads();
+    }
+    if (t < 32) {
+      // inverse CDF over the kept candidates: lane l owns positions 4l..4l+3
+      const int lane = t;
+      float w[4], acc[4], a = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int i = 4 * lane + r;
+        w[r] = (i < static_cast<int>(n) && sh.keep[i]) ? __uint_as_float(sh.cand[i].z) : 0.0f;
+        a = __fadd_rn(a, w[r]);
+        acc[r] = a;
+      }
+      float inc = a;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float nb = __shfl_up_sync(FULL, inc, o);
+        if (lane >= o) inc = __fadd_rn(inc, nb);
+      }
+      float pre = __shfl_up_sync(FULL, inc, 1);
+      if (lane == 0) pre = 0.0f;
+      const float W = __shfl_sync(FULL, inc, 31);
+      const float thr = __fmul_rn(c.u, W);
+      int r_first = -1;
+#pragma unroll
+      for (int r = 3; r >= 0; --r)
+        if (w[r] > 0.0f && __fadd_rn(pre, acc[r]) > thr) r_first = r;
+      const unsigned hit = __ballot_sync(FULL, r_first >= 0);
+      int src, rsel;
+      bool fallback = false;
+      if (hit) {
+        src = __ffs(hit) - 1;
+        rsel = __shfl_sync(FULL, r_first, src);
+      } else {
+        int r_last = -1;
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          if (w[r] > 0.0f) r_last = r;
+        const unsigned any = __ballot_sync(FULL, r_last >= 0);
+        src = any ? 31 - __clz(any) : 0;
+        rsel = any ? __shfl_sync(FULL, r_last, src) : 0;
+        fallback = true;
+      }
+      if (lane == src) {
+        const int i = 4 * lane + rsel;
+        float cdf = pre, prev = pre;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          if (r == rsel) cdf = __fadd_rn(pre, acc[r]);
+          if (r < rsel) prev = __fadd_rn(pre, acc[r]);
+        }
+        int fl = fallback ? Q3S_ROW_FALLBACK : 0;
+        const float tol = BOUNDARY_EPS * W;
+        if ((__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol)) fl |= Q3S_ROW_DRAW_BOUNDARY;
+        if (fl) atomicOr(&sh.flags, fl);
+        sh.sel_u[3] = sh.cand[i].y;
+      }
+    }
+    __syncthreads();
+    const int id = static_cast<int>(sh.sel_u[3]);
+    flags = sh.flags;
+    if (processed) {
+      uint32_t p2 = pos0;
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        if (!((vmask >> j) & 1u)) continue;
+        float out = -INFINITY;
+        if ((smask >> j) & 1u) {
+          if (sh.keep[p2]) out = v[j];
+          ++p2;
+        }
+        processed[v0 + j] = out;
+      }
+    }
+    return id;
+  }
+
+  // ---- many survivors (top-k off): block-wide top-p and draw -------------
+#pragma unroll
+  for (int j = 0; j < E; ++j) key[j] = f2key(v[j]);
   if (c.top_p < 1.0f) {
     // HF TopPLogitsWarper over a stable ascending order (value asc, index
     // asc): remove an entry when the softmax mass at-or-below it is <= 1-p;
     // the ascending-last entry always stays.
     const float frac = __fsub_rn(1.0f, c.top_p);
-    uint32_t n;
-    const uint32_t pos0 = block_excl_scan_u<NT>(__popc(smask), n, sh);
-    bool near = false;
-    if (n <= static_cast<uint32_t>(NT)) {
-      uint32_t pos = pos0;
-#pragma unroll
-      for (int j = 0; j < E; ++j)
-        if ((smask >> j) & 1u) {
-          sh.cand_k[pos] = key[j];
-          sh.cand_i[pos] = v0 + j;
-          sh.cand_w[pos] = softmax_weight(s[j], m);
-          ++pos;
-        }
-      __syncthreads();
-      float wc = 0.0f, cum = 0.0f;
-      int after = 0;
-      if (t < static_cast<int>(n)) {
-        const uint32_t kc = sh.cand_k[t];
-        const int ic = sh.cand_i[t];
-        wc = sh.cand_w[t];
-        for (int o = 0; o < static_cast<int>(n); ++o) {
-          const uint32_t ko = sh.cand_k[o];
-          const int io = sh.cand_i[o];
-          if (ko < kc || (ko == kc && io <= ic))
-            cum = __fadd_rn(cum, sh.cand_w[o]);
-          else
-            ++after;
-        }
-      }
-      const float Z = block_sum_f<NT>(wc, sh);
-      const float thr = __fmul_rn(frac, Z);
-      if (t < static_cast<int>(n)) {
-        sh.cand_keep[t] = (after == 0) || !(cum <= thr);
-        near = (after != 0) && fabsf(__fsub_rn(cum, thr)) < BOUNDARY_EPS * Z;
-      }
-      if (__syncthreads_or(near)) flags |= Q3S_ROW_TOPP_BOUNDARY;
-      uint32_t nm = 0;
-      pos = pos0;
-#pragma unroll
-      for (int j = 0; j < E; ++j)
-        if ((smask >> j) & 1u) {
-          if (sh.cand_keep[pos]) nm |= 1u << j;
-          ++pos;
-        }
-      smask = nm;
-      __syncthreads();  // cand_* reused by later phases
-    } else {
-      unsigned long long q[E], lq = 0;
+    {
+      float w[E];
+      unsigned long long lq = 0;
 #pragma unroll
       for (int j = 0; j < E; ++j) {
-        q[j] = ((smask >> j) & 1u)
-                   ? __float2ull_rn(__fmul_rn(softmax_weight(s[j], m), static_cast<float>(1ull << MASS_BITS)))
-                   : 0ull;
-        lq += q[j];
+        w[j] = ((smask >> j) & 1u) ? softmax_weight(v[j], m) : 0.0f;
+        lq += ((smask >> j) & 1u) ? mass_fixed(w[j]) : 0ull;
       }
-      const unsigned long long Zq = block_sum_q<NT>(lq, sh);
+      const unsigned long long Zq = block_sum_q<NT, E>(lq, sh, rb);
       const unsigned long long tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
       if (tau >= Zq) {
         // everything but the ascending-last entry goes
         int last = -1;
 #pragma unroll
         for (int j = 0; j < E; ++j)
-          if (((smask >> j) & 1u) && s[j] == m) last = v0 + j;
-        last = block_max_i<NT>(last, sh);
+          if (((smask >> j) & 1u) && v[j] == m) last = v0 + j;
+        last = block_max_i<NT, E>(last, sh, rb);
         smask = (last >= v0 && last < v0 + E) ? (1u << (last - v0)) : 0u;
       } else {
         uint32_t vstar;
         unsigned long long below;
-        select_mass_cut<NT>(key, q, smask, tau, sh, vstar, below);
+        select_mass_cut<NT, E>(key, w, smask, tau, sh, vstar, below);
         uint32_t ce = 0;
         unsigned long long qstar = 1;
 #pragma unroll
         for (int j = 0; j < E; ++j)
           if (((smask >> j) & 1u) && key[j] == vstar) {
             ++ce;
-            qstar = q[j];
+            qstar = mass_fixed(w[j]);
           }
         uint32_t cet;
-        uint32_t tr = block_excl_scan_u<NT>(ce, cet, sh);
+        uint32_t tr = block_excl_scan_u<NT, E>(ce, cet, sh, rb);
         qstar = qstar ? qstar : 1ull;
         const unsigned long long nrem = (tau - below) / qstar;  // ties removed (lowest index first)
         const unsigned long long eps = Zq / 1000000ull;
         uint32_t nm = 0;
+        bool near = false;
 #pragma unroll
         for (int j = 0; j < E; ++j) {
           if (!((smask >> j) & 1u)) continue;
@@ -391,63 +514,326 @@ Q3S_DEV int sample_core(const float (&x)[E], uint32_t vmask, int V, const RowCfg
             near = (first_kept - tau) < eps || (tau - last_removed) < eps;
           }
         }
-        if (__syncthreads_or(near)) flags |= Q3S_ROW_TOPP_BOUNDARY;
+        if (near) atomicOr(&sh.flags, Q3S_ROW_TOPP_BOUNDARY);
         smask = nm;
       }
     }
   }
 
   // inverse CDF in vocabulary order over the surviving softmax weights
-  float w[E], lc[E], lsum = 0.0f;
+  float lsum = 0.0f;
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
-    w[j] = ((smask >> j) & 1u) ? softmax_weight(s[j], m) : 0.0f;
-    lsum = __fadd_rn(lsum, w[j]);
-    lc[j] = lsum;
-  }
+  for (int j = 0; j < E; ++j) lsum = __fadd_rn(lsum, ((smask >> j) & 1u) ? softmax_weight(v[j], m) : 0.0f);
   float W;
-  const float pre = block_excl_scan_f<NT>(lsum, W, sh);
+  const float pre = block_excl_scan_f<NT, E>(lsum, W, sh, rb);
   const float thr = __fmul_rn(c.u, W);
   int first = 0x7fffffff;
+  {
+    float acc = 0.0f;
 #pragma unroll
-  for (int j = E - 1; j >= 0; --j)
-    if (w[j] > 0.0f && __fadd_rn(pre, lc[j]) > thr) first = v0 + j;
-  int id = block_min_i<NT>(first, sh);
+    for (int j = 0; j < E; ++j) {
+      const float w = ((smask >> j) & 1u) ? softmax_weight(v[j], m) : 0.0f;
+      acc = __fadd_rn(acc, w);
+      if (first == 0x7fffffff && w > 0.0f && __fadd_rn(pre, acc) > thr) first = v0 + j;
+    }
+  }
+  int id = block_min_i<NT, E>(first, sh, rb);
+  bool fallback = false;
   if (id == 0x7fffffff) {
     int last = -1;
 #pragma unroll
     for (int j = 0; j < E; ++j)
-      if (w[j] > 0.0f) last = v0 + j;
-    id = block_max_i<NT>(last, sh);
-    flags |= Q3S_ROW_FALLBACK;
+      if ((smask >> j) & 1u) last = v0 + j;
+    id = block_max_i<NT, E>(last, sh, rb);
+    fallback = true;
   }
-  bool near = false;
-  float prev = pre;
+  flags = sh.flags | (fallback ? Q3S_ROW_FALLBACK : 0);
+  if (id >= v0 && id < v0 + E) {
+    // owner: is the draw within 1e-6 (relative) of a CDF edge?
+    float acc = 0.0f, prev = pre, cdf = pre;
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
-    const float cdf = __fadd_rn(pre, lc[j]);
-    if (v0 + j == id) {
-      const float tol = BOUNDARY_EPS * W;
-      near = (__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol);
+    for (int j = 0; j < E; ++j) {
+      const float w = ((smask >> j) & 1u) ? softmax_weight(v[j], m) : 0.0f;
+      acc = __fadd_rn(acc, w);
+      const float cur = __fadd_rn(pre, acc);
+      if (v0 + j == id) cdf = cur;
+      if (v0 + j < id) prev = cur;
     }
-    prev = cdf;
+    const float tol = BOUNDARY_EPS * W;
+    if ((__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol)) flags |= Q3S_ROW_DRAW_BOUNDARY;
   }
-  if (__syncthreads_or(near)) flags |= Q3S_ROW_DRAW_BOUNDARY;
   if (processed) {
 #pragma unroll
     for (int j = 0; j < E; ++j)
-      if ((vmask >> j) & 1u) processed[v0 + j] = ((smask >> j) & 1u) ? s[j] : -INFINITY;
+      if ((vmask >> j) & 1u) processed[v0 + j] = ((smask >> j) & 1u) ? v[j] : -INFINITY;
   }
   return id;
+}
+
+// Full sampler for one row.  x: logits after suppress and the EOS gate, before
+// the repetition penalty, which applies to the entries flagged in `pmask`
+// (x > 0 ? x / pen : x * pen).  Every thread returns the same id; `flags`
+// is complete in the thread that owns the id (v0 <= id < v0+E).
+//
+// Rows that keep a few entries (top-k rows, Gumbel exactly-K rows, greedy
+// rows) select on approximate keys -- the penalty division replaced by a
+// multiply with RN(1/pen), within a few ulps of it -- and resolve exactly on
+// a small candidate set: every entry whose approximate key is within 40 ulps
+// of the selected threshold or above.  That set holds every entry of the
+// exact top K (keys move by at most ~4 ulps), every entry below it sits at
+// least 8 ulps under the exact K-th value, so no temperature-quotient tie can
+// reach outside the set, and only its entries are divided exactly.  Rows that
+// keep the whole vocabulary, or whose candidate set overflows (massive ties),
+// take sample_exact.
+template <int NT, int E, int MODE>
+Q3S_DEV int sample_core(float (&x)[E], uint32_t vmask, uint32_t pmask, float pen, int V, const RowCfg& c,
+                        Scratch<NT, E>& sh, float* processed, int& flags, uint32_t& err) {
+  const int t = threadIdx.x;
+  const int v0 = t * E;
+  // negative penalised entries are exact products; dmask = entries still to divide
+  uint32_t dmask = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if ((pmask >> j) & 1u) {
+      if (x[j] > 0.0f)
+        dmask |= 1u << j;
+      else
+        x[j] = __fmul_rn(x[j], pen);
+    }
+  const bool topk_row = c.greedy || MODE == Q3S_DRAW_GUMBEL || (c.k > 0 && c.k < V);
+  const bool window_ok = c.greedy || MODE == Q3S_DRAW_GUMBEL || (c.T >= 0x1p-20f && c.T <= 0x1p20f);
+  if (!topk_row || !window_ok) {
+#pragma unroll
+    for (int j = 0; j < E; ++j)
+      if ((dmask >> j) & 1u) x[j] = __fdiv_rn(x[j], pen);
+    return sample_exact<NT, E, MODE>(x, vmask, V, c, sh, processed, flags, err);
+  }
+
+  int rb = 0;
+  flags = 0;
+  if (t == 0) sh.flags = 0;  // published by the first barrier below
+  const int K = c.greedy ? 1 : c.k;
+  if (MODE == Q3S_DRAW_GUMBEL && !c.greedy) {
+    for (int r = t; r < K; r += NT) sh.noise[r] = __ldg(c.noise + r);
+  }
+  uint32_t key[E];
+  {
+    const float rpen = __frcp_rn(pen);
+#pragma unroll
+    for (int j = 0; j < E; ++j) key[j] = f2key(((dmask >> j) & 1u) ? __fmul_rn(x[j], rpen) : x[j]);
+  }
+  const uint32_t thr = select_threshold<NT, E>(key, vmask, K, FINISH + K / 2, sh, rb);
+  const uint32_t lo = thr > 40u ? thr - 40u : 0u;
+  uint32_t cmask = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if (((vmask >> j) & 1u) && key[j] >= lo) cmask |= 1u << j;
+  uint32_t n;
+  const uint32_t pos0 = block_excl_scan_u<NT, E>(__popc(cmask), n, sh, rb);
+  if (n > static_cast<uint32_t>(CAND)) {
+#pragma unroll
+    for (int j = 0; j < E; ++j)
+      if ((dmask >> j) & 1u) x[j] = __fdiv_rn(x[j], pen);
+    __syncthreads();  // shared state of this path is reused by sample_exact
+    return sample_exact<NT, E, MODE>(x, vmask, V, c, sh, processed, flags, err);
+  }
+  // candidate records in vocabulary order: {s or x' bits, index, x' bits, weight bits}
+  const int n4 = (static_cast<int>(n) + 3) & ~3;
+  {
+    uint32_t pos = pos0;
+#pragma unroll
+    for (int j = 0; j < E; ++j)
+      if ((cmask >> j) & 1u) {
+        const float xe = ((dmask >> j) & 1u) ? __fdiv_rn(x[j], pen) : x[j];
+        sh.cand[pos] = make_uint4(0u, static_cast<uint32_t>(v0 + j), __float_as_uint(xe), 0u);
+        ++pos;
+      }
+    for (int i = static_cast<int>(n) + t; i < n4; i += NT)
+      sh.cand[i] = make_uint4(0xff800000u, 0x7fffffffu, 0xff800000u, 0u);  // -inf, never outranks
+  }
+  __syncthreads();
+
+  if (MODE == Q3S_DRAW_GUMBEL || c.greedy) {
+    // exactly-K by (x' desc, index asc) (talker_unified_modules.py:415,
+    // utils.py:1189); score x'/T + noise[rank]; argmax, lowest rank on ties
+    float bs = -INFINITY;
+    int br = 0x7fffffff, bid = 0x7fffffff;
+    for (int i = t; i < static_cast<int>(n); i += NT) {
+      const uint4 me = sh.cand[i];
+      const float xi = __uint_as_float(me.z);
+      const int ii = static_cast<int>(me.y);
+      int rank = 0;
+      for (int o = 0; o < n4; o += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint4 ot = sh.cand[o + u];
+          const float xo = __uint_as_float(ot.z);
+          rank += (xo > xi) | ((xo == xi) & (static_cast<int>(ot.y) < ii));
+        }
+      }
+      if (rank < K) {
+        const float score = c.greedy ? -static_cast<float>(rank)
+                                     : __fadd_rn(__fdiv_rn(xi, c.T), sh.noise[rank]);
+        if (arg_better(score, rank, bs, br)) {
+          bs = score;
+          br = rank;
+          bid = ii;
+        }
+      }
+    }
+    const int id = block_argmax<NT, E>(bs, br, bid, sh, rb);
+    flags = c.greedy ? Q3S_ROW_GREEDY : 0;
+    if (processed) {
+#pragma unroll
+      for (int j = 0; j < E; ++j)
+        if ((vmask >> j) & 1u) processed[v0 + j] = ((dmask >> j) & 1u) ? __fdiv_rn(x[j], pen) : x[j];
+    }
+    return id;
+  }
+
+  if constexpr (MODE == Q3S_DRAW_ICDF) {
+    // ---- icdf: HF top-k survivors among the candidates, top-p, draw --------
+    // s = x'/T; an entry survives when fewer than k entries have a larger s
+    for (int i = t; i < static_cast<int>(n); i += NT)
+      sh.cand[i].x = __float_as_uint(__fdiv_rn(__uint_as_float(sh.cand[i].z), c.T));
+    __syncthreads();
+    for (int i = t; i < static_cast<int>(n); i += NT) {
+      const float si = __uint_as_float(sh.cand[i].x);
+      int above = 0;
+      float m = -INFINITY;
+      for (int o = 0; o < n4; o += 4) {
+  #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float so = __uint_as_float(sh.cand[o + u].x);
+          above += so > si;
+          m = fmaxf(m, so);
+        }
+      }
+      const bool surv = above < K;
+      sh.surv[i] = surv;
+      sh.keep[i] = surv;
+      sh.cand[i].w = __float_as_uint(surv ? softmax_weight(si, m) : 0.0f);
+    }
+    __syncthreads();
+    if (c.top_p < 1.0f) {
+      // HF TopPLogitsWarper over a stable ascending order (value asc, index
+      // asc): remove a survivor when the softmax mass at-or-below it is <= 1-p;
+      // the ascending-last survivor always stays.
+      const float frac = __fsub_rn(1.0f, c.top_p);
+      for (int i = t; i < static_cast<int>(n); i += NT) {
+        if (!sh.surv[i]) continue;
+        const uint4 me = sh.cand[i];
+        const float si = __uint_as_float(me.x);
+        const int ii = static_cast<int>(me.y);
+        float cum = 0.0f, Z = 0.0f;
+        int after = 0;
+        for (int o = 0; o < n4; o += 4) {
+  #pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint4 ot = sh.cand[o + u];
+            const float so = __uint_as_float(ot.x);
+            const float w = __uint_as_float(ot.w);
+            const bool sv = o + u < static_cast<int>(n) && sh.surv[o + u];
+            const bool before = (so < si) | ((so == si) & (static_cast<int>(ot.y) <= ii));
+            cum = __fadd_rn(cum, (sv && before) ? w : 0.0f);
+            Z = __fadd_rn(Z, sv ? w : 0.0f);
+            after += sv && !before;
+          }
+        }
+        const float thr_m = __fmul_rn(frac, Z);
+        sh.keep[i] = (after == 0) || !(cum <= thr_m);
+        if (after != 0 && fabsf(__fsub_rn(cum, thr_m)) < BOUNDARY_EPS * Z) atomicOr(&sh.flags, Q3S_ROW_TOPP_BOUNDARY);
+      }
+      __syncthreads();
+    }
+    if (t < 32) {
+      // inverse CDF over the kept candidates (vocabulary order): lane l owns
+      // positions [l*P, l*P + P) for P = ceil(n/32) <= 16
+      const int lane = t;
+      const int P = (static_cast<int>(n) + 31) / 32;
+      float a = 0.0f;
+      for (int r = 0; r < P; ++r) {
+        const int i = lane * P + r;
+        if (i < static_cast<int>(n) && sh.keep[i]) a = __fadd_rn(a, __uint_as_float(sh.cand[i].w));
+      }
+      float inc = a;
+  #pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float nb = __shfl_up_sync(FULL, inc, o);
+        if (lane >= o) inc = __fadd_rn(inc, nb);
+      }
+      float pre = __shfl_up_sync(FULL, inc, 1);
+      if (lane == 0) pre = 0.0f;
+      const float W = __shfl_sync(FULL, inc, 31);
+      const float thr_u = __fmul_rn(c.u, W);
+      int r_first = -1, r_last = -1;
+      float acc = 0.0f;
+      for (int r = 0; r < P; ++r) {
+        const int i = lane * P + r;
+        const float w = (i < static_cast<int>(n) && sh.keep[i]) ? __uint_as_float(sh.cand[i].w) : 0.0f;
+        acc = __fadd_rn(acc, w);
+        if (w > 0.0f) {
+          r_last = r;
+          if (r_first < 0 && __fadd_rn(pre, acc) > thr_u) r_first = r;
+        }
+      }
+      const unsigned hit = __ballot_sync(FULL, r_first >= 0);
+      int src, rsel;
+      bool fallback = false;
+      if (hit) {
+        src = __ffs(hit) - 1;
+        rsel = __shfl_sync(FULL, r_first, src);
+      } else {
+        const unsigned any = __ballot_sync(FULL, r_last >= 0);
+        src = any ? 31 - __clz(any) : 0;
+        rsel = any ? __shfl_sync(FULL, r_last, src) : 0;
+        fallback = true;
+      }
+      if (lane == src) {
+        float cdf = pre, prev = pre, a2 = 0.0f;
+        for (int r = 0; r <= rsel; ++r) {
+          const int i = lane * P + r;
+          const float w = (i < static_cast<int>(n) && sh.keep[i]) ? __uint_as_float(sh.cand[i].w) : 0.0f;
+          a2 = __fadd_rn(a2, w);
+          if (r < rsel) prev = __fadd_rn(pre, a2);
+          cdf = __fadd_rn(pre, a2);
+        }
+        int fl = fallback ? Q3S_ROW_FALLBACK : 0;
+        const float tol = BOUNDARY_EPS * W;
+        if ((__fsub_rn(cdf, thr_u) < tol) || (__fsub_rn(thr_u, prev) < tol)) fl |= Q3S_ROW_DRAW_BOUNDARY;
+        if (fl) atomicOr(&sh.flags, fl);
+        sh.sel_u[3] = sh.cand[lane * P + rsel].y;
+      }
+    }
+    __syncthreads();
+    const int id = static_cast<int>(sh.sel_u[3]);
+    flags = sh.flags;
+    if (processed) {
+      uint32_t p2 = pos0;
+  #pragma unroll
+      for (int j = 0; j < E; ++j) {
+        if (!((vmask >> j) & 1u)) continue;
+        float out = -INFINITY;
+        if ((cmask >> j) & 1u) {
+          if (sh.keep[p2]) out = __uint_as_float(sh.cand[p2].x);
+          ++p2;
+        }
+        processed[v0 + j] = out;
+      }
+    }
+    return id;
+  } else {
+    return 0;  // not reached: gumbel rows return above
+  }
 }
 
 // ---------------------------------------------------------------------------
 // one sampling step, one CTA per row
 // ---------------------------------------------------------------------------
 
-template <int NT, bool BF16>
+template <int NT, int E, bool BF16, int MODE>
 __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
-  __shared__ Scratch<NT> sh;
+  __shared__ Scratch<NT, E> sh;
   const int b = blockIdx.x;
   const int t = threadIdx.x;
   const int v0 = t * E;
@@ -458,15 +844,18 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
   const int shift = a.col_shift ? norm_shift(__ldg(a.col_shift + b), V) : 0;
   float x[E];
   uint32_t vmask;
-  load_logits8<BF16>(a.logits, static_cast<int64_t>(b) * a.row_stride, V, v0, shift, a.vec_logits, x,
-                     vmask);
-
+  load_logits<BF16, E>(a.logits, static_cast<int64_t>(b) * a.row_stride, V, v0, shift, a.vec_logits, x, vmask);
+  int o0 = 0, o1 = 0;
+  if (a.history) {
+    o0 = __ldg(a.offsets + b);
+    o1 = __ldg(a.offsets + b + 1);
+  }
   uint32_t app = 0;
   if (a.token_counts) {
     const int64_t* tc = a.token_counts + static_cast<int64_t>(b) * a.tc_stride + v0;
     if (a.vec_counts && v0 + E <= V) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < E / 2; ++i) {
         const uint4 r = ld_stream16(tc + 2 * i);
         const int64_t c0 = static_cast<int64_t>((static_cast<uint64_t>(r.y) << 32) | r.x);
         const int64_t c1 = static_cast<int64_t>((static_cast<uint64_t>(r.w) << 32) | r.z);
@@ -482,12 +871,7 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
   uint32_t sup = 0;
   if (a.suppress) {
     if (a.vec_suppress && v0 + E <= V) {
-      const uint2 m = __ldg(reinterpret_cast<const uint2*>(a.suppress + v0));
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        sup |= (((m.x >> (8 * j)) & 0xffu) ? 1u : 0u) << j;
-        sup |= (((m.y >> (8 * j)) & 0xffu) ? 1u : 0u) << (j + 4);
-      }
+      sup = bytes_to_mask<E>(a.suppress + v0);
     } else {
 #pragma unroll
       for (int j = 0; j < E; ++j)
@@ -500,55 +884,75 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
   const int kk = (a.mode == Q3S_DRAW_ICDF && a.top_k) ? __ldg(a.top_k + b) : a.K;
   const int min_new = a.min_new ? __ldg(a.min_new + b) : a.min_new_default;
   const float u = a.uniforms ? __ldg(a.uniforms + b) : 0.0f;
+  clear_hist<NT, E>(sh);
+  // suppress now: waiting for the logits here overlaps the offsets round trip
+  // (otherwise the compiler may sink the logits load past the history phase)
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if ((sup >> j) & 1u) x[j] = NEG_SUPPRESS;
 
   int hist_len = 0;
   if (a.history) {
-    int o0 = __ldg(a.offsets + b), o1 = __ldg(a.offsets + b + 1);
     if (o0 < 0 || o1 < o0 || static_cast<int64_t>(o1) > a.history_len) {
       err |= Q3S_DEVERR_OFFSETS;
       o0 = o1 = 0;
     }
     hist_len = o1 - o0;
-    *reinterpret_cast<uint2*>(&sh.seen[v0]) = make_uint2(0u, 0u);
-    __syncthreads();
-    // presence scatter: racing stores of the same byte need no atomics
-    for (int i = o0 + t; i < o1; i += 4 * NT) {
-      int id[4];
-      bool in[4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        in[r] = i + r * NT < o1;
-        id[r] = in[r] ? __ldg(a.history + i + r * NT) : 0;
+    for (int c = 0; c < E / 8; ++c) *reinterpret_cast<uint2*>(&sh.seen[v0 + 8 * c]) = make_uint2(0u, 0u);
+    __syncthreads();
+    // presence scatter (racing stores of the same byte need no atomics):
+    // 16-byte loads over the aligned middle of the row's ids, scalar loads for
+    // the ragged head [o0, mid0) and tail [mid1, o1); each thread issues up to
+    // U loads before its first store, so the ids arrive in one round trip
+    const int32_t* h = a.history;
+    int mid0 = o0, mid1 = o0;
+    if (a.vec_history) {
+      mid0 = min(o1, (o0 + 3) & ~3);
+      mid1 = mid0 + ((o1 - mid0) & ~3);
+    }
+    const int nhead = mid0 - o0;
+    const int nrest = nhead + (o1 - mid1);
+    const int nwork = nrest + (mid1 - mid0) / 4;  // scalar ids first, then 16-byte chunks
+    constexpr int U = 8;
+    for (int r = t; r < nwork; r += U * NT) {
+      int4 ids[U];
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        const int rr = r + q * NT;
+        ids[q] = make_int4(-1, -1, -1, -1);
+        if (rr < nrest)
+          ids[q].x = __ldg(h + (rr < nhead ? o0 + rr : mid1 + (rr - nhead)));
+        else if (rr < nwork)
+          ids[q] = __ldg(reinterpret_cast<const int4*>(h + mid0) + (rr - nrest));
       }
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        if (!in[r]) continue;
-        if (static_cast<unsigned>(id[r]) < static_cast<unsigned>(V))
-          sh.seen[id[r]] = 1;
-        else
-          err |= Q3S_DEVERR_HISTORY_ID;
+      for (int q = 0; q < U; ++q) {
+        const int rr = r + q * NT;
+        if (rr >= nwork) continue;
+        const int nid = rr < nrest ? 1 : 4;
+        const int idv[4] = {ids[q].x, ids[q].y, ids[q].z, ids[q].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (i >= nid) break;
+          if (static_cast<unsigned>(idv[i]) < static_cast<unsigned>(V))
+            sh.seen[idv[i]] = 1;
+          else
+            err |= Q3S_DEVERR_HISTORY_ID;
+        }
       }
     }
     __syncthreads();
-    const uint2 f = *reinterpret_cast<const uint2*>(&sh.seen[v0]);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      app |= (((f.x >> (8 * j)) & 0xffu) ? 1u : 0u) << j;
-      app |= (((f.y >> (8 * j)) & 0xffu) ? 1u : 0u) << (j + 4);
-    }
+    app |= bytes_to_mask<E>(&sh.seen[v0]);
   }
   const int cur = a.cur_len ? __ldg(a.cur_len + b) : hist_len;
   const bool gate = a.eos_id >= 0 && a.eos_id < V && cur < min_new;
 
-  // suppress (-1e9) -> presence penalty -> EOS gate
+  // EOS gate (-inf is unchanged by the penalty that sample_core applies)
+  if (gate && a.eos_id >= v0 && a.eos_id < v0 + E) {
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
-    if (!((vmask >> j) & 1u)) continue;
-    float v = x[j];
-    if ((sup >> j) & 1u) v = NEG_SUPPRESS;
-    if ((app >> j) & 1u) v = (v > 0.0f) ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
-    if (gate && v0 + j == a.eos_id) v = -INFINITY;
-    x[j] = v;
+    for (int j = 0; j < E; ++j)
+      if (v0 + j == a.eos_id) x[j] = -INFINITY;
   }
 
   RowCfg c;
@@ -561,9 +965,9 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
   c.noise = a.noise ? a.noise + static_cast<int64_t>(b) * a.noise_stride : nullptr;
   float* proc = a.processed ? a.processed + static_cast<int64_t>(b) * a.proc_stride : nullptr;
   int flags;
-  const int id = sample_core<NT>(x, vmask, V, c, sh, proc, flags, err);
+  const int id = sample_core<NT, E, MODE>(x, vmask, app & vmask, pen, V, c, sh, proc, flags, err);
 
-  const bool owner = id >= v0 && id < v0 + E;
+  const bool owner = (id >= v0 && id < v0 + E) || (t == 0 && (id < 0 || id >= V));
   if (owner) {
     if (a.ids64) a.ids64[b] = id;
     if (a.ids32) a.ids32[b] = id;
@@ -572,7 +976,7 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
   if (a.counts_out) {
     int64_t* co = a.counts_out + static_cast<int64_t>(b) * a.co_stride;
     if (a.counts_out == a.token_counts && a.co_stride == a.tc_stride) {
-      if (owner) co[id] += 1;  // in-place: the row was read before any write
+      if (owner && id >= 0 && id < V) co[id] += 1;  // in-place: the row was read before any write
     } else {
       const int64_t* tc = a.token_counts + static_cast<int64_t>(b) * a.tc_stride;
 #pragma unroll
@@ -620,9 +1024,9 @@ Q3S_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-template <int NT, bool BF16>
+template <int NT, int E, bool BF16, int MODE>
 __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
-  __shared__ Scratch<NT> sh;
+  __shared__ Scratch<NT, E> sh;
   __shared__ __align__(8) uint64_t bars[MAX_NBUF];
   extern __shared__ __align__(128) unsigned char ring[];
   const int t = threadIdx.x;
@@ -643,6 +1047,7 @@ __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
     bulk_g2s(ring + static_cast<size_t>(slot) * a.row_bytes, src, a.row_bytes, &bars[slot]);
   };
 
+  clear_hist<NT, E>(sh);
   if (a.bulk) {
     if (t == 0) {
       for (int s = 0; s < a.nbuf; ++s) mbar_init(&bars[s], 1);
@@ -692,8 +1097,11 @@ __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
         __syncthreads();  // every thread has read the slot
         if (t == 0 && g + a.nbuf < nitems) issue(g + a.nbuf);
       } else {
-        load_logits8<BF16>(a.logits, static_cast<int64_t>(j) * a.stage_stride + static_cast<int64_t>(b) * a.row_stride,
-                           V, v0, shift, false, x, vmask);
+        // every thread is done with the previous stage's shared state
+        __syncthreads();
+        load_logits<BF16, E>(a.logits,
+                             static_cast<int64_t>(j) * a.stage_stride + static_cast<int64_t>(b) * a.row_stride, V, v0,
+                             shift, false, x, vmask);
       }
       RowCfg c;
       c.mode = a.mode;
@@ -702,12 +1110,13 @@ __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
       c.k = a.K;
       c.top_p = top_p;
       c.u = a.uniforms ? __ldg(a.uniforms + static_cast<int64_t>(b) * S + j) : 0.0f;
-      c.noise = a.noise ? a.noise + static_cast<int64_t>(b) * a.noise_row_stride + static_cast<int64_t>(j) * a.noise_stage_stride
+      c.noise = a.noise ? a.noise + static_cast<int64_t>(b) * a.noise_row_stride +
+                              static_cast<int64_t>(j) * a.noise_stage_stride
                         : nullptr;
       int flags;
       uint32_t err = 0;
-      const int id = sample_core<NT>(x, vmask, V, c, sh, nullptr, flags, err);
-      if (t == 0) {
+      const int id = sample_core<NT, E, MODE>(x, vmask, 0u, 1.0f, V, c, sh, nullptr, flags, err);
+      if (id >= v0 && id < v0 + E) {  // the owner holds the complete flags
         a.ids_out[static_cast<int64_t>(b) * S + j] = id;
         if (a.row_flags) a.row_flags[static_cast<int64_t>(b) * S + j] = flags;
       }
@@ -742,20 +1151,29 @@ q3s_status ok() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int pick_threads(int V) {
-  const int need = (V + q3s::E - 1) / q3s::E;
-  static const int sizes[] = {64, 128, 256, 384, 512, 768, 1024};
-  for (int s : sizes)
-    if (s >= need) return s;
-  return -1;
+// Threads per row and entries per thread for a vocabulary size: 8 entries per
+// thread (one 16-byte bf16 load) up to V = 4096.
+bool pick_shape(int V, int& nt, int& e) {
+  if (V <= 512) { nt = 64; e = 8; }
+  else if (V <= 1024) { nt = 128; e = 8; }
+  else if (V <= 2048) { nt = 256; e = 8; }
+  else if (V <= 3072) { nt = 384; e = 8; }
+  else if (V <= 4096) { nt = 512; e = 8; }
+  else if (V <= Q3S_MAX_VOCAB) { nt = 512; e = 16; }
+  else return false;
+  return true;
 }
 
-template <int NT>
+template <int NT, int E>
 q3s_status launch_rows(const q3s::SampleArgs& a, bool bf16, cudaStream_t st) {
-  if (bf16)
-    q3s::sample_rows_kernel<NT, true><<<a.B, NT, 0, st>>>(a);
-  else
-    q3s::sample_rows_kernel<NT, false><<<a.B, NT, 0, st>>>(a);
+  const bool g = a.mode == Q3S_DRAW_GUMBEL;
+  if (bf16) {
+    if (g) q3s::sample_rows_kernel<NT, E, true, Q3S_DRAW_GUMBEL><<<a.B, NT, 0, st>>>(a);
+    else q3s::sample_rows_kernel<NT, E, true, Q3S_DRAW_ICDF><<<a.B, NT, 0, st>>>(a);
+  } else {
+    if (g) q3s::sample_rows_kernel<NT, E, false, Q3S_DRAW_GUMBEL><<<a.B, NT, 0, st>>>(a);
+    else q3s::sample_rows_kernel<NT, E, false, Q3S_DRAW_ICDF><<<a.B, NT, 0, st>>>(a);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample launch failed: %s", cudaGetErrorString(e));
   return ok();
@@ -773,10 +1191,10 @@ int device_sm_count() {
   return cache[dev];
 }
 
-template <int NT, bool BF16>
+template <int NT, int E, bool BF16, int MODE>
 q3s_status launch_cp_t(const q3s::CpArgs& a, cudaStream_t st) {
   const size_t dyn = a.bulk ? static_cast<size_t>(a.nbuf) * a.row_bytes : 0;
-  auto kern = q3s::cp_frame_kernel<NT, BF16>;
+  auto kern = q3s::cp_frame_kernel<NT, E, BF16, MODE>;
   if (dyn > 0) {
     // static + dynamic shared memory may pass the 48 KB default: opt in.
     // Idempotent per (kernel, device); the value only ever grows.
@@ -799,9 +1217,11 @@ q3s_status launch_cp_t(const q3s::CpArgs& a, cudaStream_t st) {
   return ok();
 }
 
-template <int NT>
+template <int NT, int E>
 q3s_status launch_cp(const q3s::CpArgs& a, bool bf16, cudaStream_t st) {
-  return bf16 ? launch_cp_t<NT, true>(a, st) : launch_cp_t<NT, false>(a, st);
+  if (a.mode == Q3S_DRAW_GUMBEL)
+    return bf16 ? launch_cp_t<NT, E, true, Q3S_DRAW_GUMBEL>(a, st) : launch_cp_t<NT, E, false, Q3S_DRAW_GUMBEL>(a, st);
+  return bf16 ? launch_cp_t<NT, E, true, Q3S_DRAW_ICDF>(a, st) : launch_cp_t<NT, E, false, Q3S_DRAW_ICDF>(a, st);
 }
 
 }  // namespace
@@ -862,8 +1282,8 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
     if (!d->uniforms && !all_greedy)
       return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample: icdf mode needs uniforms");
   }
-  const int nt = pick_threads(V);
-  if (nt < 0) return fail(Q3S_ERR_UNSUPPORTED, "q3s_sample: vocab %d too large", V);
+  int nt = 0, ne = 0;
+  if (!pick_shape(V, nt, ne)) return fail(Q3S_ERR_UNSUPPORTED, "q3s_sample: vocab %d too large", V);
   const bool bf16 = d->logits_dtype == Q3S_DTYPE_BF16;
   const int esz = bf16 ? 2 : 4;
 
@@ -907,16 +1327,16 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
   a.vec_logits = aligned16(d->logits) && ((d->logits_row_stride * esz) % 16 == 0);
   a.vec_counts = d->token_counts && aligned16(d->token_counts) && (d->token_counts_row_stride % 2 == 0);
   a.vec_suppress = d->suppress_mask && ((reinterpret_cast<uintptr_t>(d->suppress_mask) & 7u) == 0);
+  a.vec_history = d->history && aligned16(d->history);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (ne == 16) return launch_rows<512, 16>(a, bf16, st);
   switch (nt) {
-    case 64: return launch_rows<64>(a, bf16, st);
-    case 128: return launch_rows<128>(a, bf16, st);
-    case 256: return launch_rows<256>(a, bf16, st);
-    case 384: return launch_rows<384>(a, bf16, st);
-    case 512: return launch_rows<512>(a, bf16, st);
-    case 768: return launch_rows<768>(a, bf16, st);
-    default: return launch_rows<1024>(a, bf16, st);
+    case 64: return launch_rows<64, 8>(a, bf16, st);
+    case 128: return launch_rows<128, 8>(a, bf16, st);
+    case 256: return launch_rows<256, 8>(a, bf16, st);
+    case 384: return launch_rows<384, 8>(a, bf16, st);
+    default: return launch_rows<512, 8>(a, bf16, st);
   }
 }
 
@@ -957,8 +1377,8 @@ q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
     if (!d->uniforms && !all_greedy)
       return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample_cp_frame: icdf mode needs uniforms");
   }
-  const int nt = pick_threads(V);
-  if (nt < 0) return fail(Q3S_ERR_UNSUPPORTED, "q3s_sample_cp_frame: vocab %d too large", V);
+  int nt = 0, ne = 0;
+  if (!pick_shape(V, nt, ne)) return fail(Q3S_ERR_UNSUPPORTED, "q3s_sample_cp_frame: vocab %d too large", V);
   const bool bf16 = d->logits_dtype == Q3S_DTYPE_BF16;
   const int esz = bf16 ? 2 : 4;
 
@@ -992,14 +1412,13 @@ q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
   a.nbuf = a.bulk ? std::max(2, std::min(q3s::MAX_NBUF, static_cast<int>((16u * 1024u) / a.row_bytes))) : 0;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (ne == 16) return launch_cp<512, 16>(a, bf16, st);
   switch (nt) {
-    case 64: return launch_cp<64>(a, bf16, st);
-    case 128: return launch_cp<128>(a, bf16, st);
-    case 256: return launch_cp<256>(a, bf16, st);
-    case 384: return launch_cp<384>(a, bf16, st);
-    case 512: return launch_cp<512>(a, bf16, st);
-    case 768: return launch_cp<768>(a, bf16, st);
-    default: return launch_cp<1024>(a, bf16, st);
+    case 64: return launch_cp<64, 8>(a, bf16, st);
+    case 128: return launch_cp<128, 8>(a, bf16, st);
+    case 256: return launch_cp<256, 8>(a, bf16, st);
+    case 384: return launch_cp<384, 8>(a, bf16, st);
+    default: return launch_cp<512, 8>(a, bf16, st);
   }
 }
 

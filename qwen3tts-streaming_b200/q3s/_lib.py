@@ -15,7 +15,7 @@ from .build import LIB_PATH
 
 Q3S_ABI_VERSION = 1
 MAX_VOCAB = 8192
-MAX_TOPK = 1024
+MAX_TOPK = 512
 MAX_CP_STAGES = 64
 
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3

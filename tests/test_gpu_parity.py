@@ -58,12 +58,21 @@ def oracle_icdf(b: workloads.Batch):
                          min_new_tokens=b.min_new_tokens.numpy(), suppress=b.suppress.numpy(), eos_id=b.eos_id)
 
 
-def assert_ids_match(ids, ref, kflags, label):
+def assert_ids_match(ids, ref, kflags, label, max_frac=None):
+    """Bit-exact ids except on boundary rows (flagged by the oracle or the
+    kernel); a boundary row that differs must still pick an id the oracle's
+    processed row kept.  ``max_frac`` bounds the boundary share for random
+    inputs (edge-case tests sit on CDF edges by construction)."""
     bnd = ref["boundary"] | ((kflags & (_lib.ROW_DRAW_BOUNDARY | _lib.ROW_TOPP_BOUNDARY)) != 0)
     bad = (ids != ref["ids"]) & ~bnd
     assert not bad.any(), f"{label}: {bad.sum()} non-boundary mismatches at rows {np.nonzero(bad)[0][:10]}"
-    assert bnd.mean() <= MAX_BOUNDARY_FRACTION + 1.0 / len(ids), f"{label}: {bnd.sum()} boundary rows"
-    return int(bnd.sum()), int(((ids != ref["ids"]) & bnd).sum())
+    diff = np.nonzero((ids != ref["ids"]) & bnd)[0]
+    if "processed" in ref:
+        for r in diff:
+            assert np.isfinite(ref["processed"][r, ids[r]]), f"{label}: row {r} drew a filtered id {ids[r]}"
+    if max_frac is not None:
+        assert bnd.mean() <= max_frac + 1.0 / len(ids), f"{label}: {bnd.sum()} boundary rows"
+    return int(bnd.sum()), int(len(diff))
 
 
 # ---------------------------------------------------------------------------
@@ -155,7 +164,7 @@ def test_configs_match_oracle(cuda_device, q3s_lib, cfg, rows):
     ids, proc, kf, err = run_icdf_batch(b, cuda_device)
     ref = oracle_icdf(b)
     assert err == 0
-    nb, nbm = assert_ids_match(ids, ref, kf, f"config {cfg}")
+    nb, nbm = assert_ids_match(ids, ref, kf, f"config {cfg}", max_frac=MAX_BOUNDARY_FRACTION)
     ok = ~(ref["boundary"] | ((kf & 3) != 0))
     assert _proc_close(proc[ok], ref["processed"][ok])
     greedy = b.temperature.numpy() <= 0
@@ -221,7 +230,7 @@ def test_vocab_sizes_and_filters(cuda_device, q3s_lib, V, k, p):
     x = (rng.standard_normal((6, V)) * 2.0).astype(np.float32)
     ids, proc, kf, err, ref = _icdf_case(cuda_device, x, T=0.8, k=k, p=p)
     assert err == 0
-    assert_ids_match(ids, ref, kf, f"V={V} k={k} p={p}")
+    assert_ids_match(ids, ref, kf, f"V={V} k={k} p={p}", max_frac=0.5)
     ok = ~(ref["boundary"] | ((kf & 3) != 0))
     assert _proc_close(proc[ok], ref["processed"][ok])
 
