@@ -186,6 +186,24 @@ int32_t q3s_abi_version(void);
  * can check its own struct layout (which: 0 = sample, 1 = cp_frame). */
 uint32_t q3s_desc_size(int32_t which);
 
+/* Kernel family for icdf steps that either family can serve (process-wide;
+ * a tuning and test knob with no counterpart in the reference interface).
+ * AUTO picks warp-per-row for large batches and CTA-per-row otherwise; the
+ * two return the same ids, except that a draw or a top-p cut within 1e-6 of a
+ * cumulative-mass edge (flagged in row_flags) may land on either side.
+ * Steps that need token_counts, col_shift, processed_logits or counts_out,
+ * Gumbel mode, or a vocabulary outside (1024, 3072] or not a multiple of 8
+ * always take CTA-per-row. */
+typedef enum {
+  Q3S_POLICY_AUTO = 0,
+  Q3S_POLICY_CTA = 1,
+  Q3S_POLICY_WARP = 2
+} q3s_kernel_policy;
+
+/* Set the policy; returns the previous one, or -1 (unchanged) for an unknown
+ * value. */
+int32_t q3s_set_kernel_policy(int32_t policy);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,72 @@
+// q3s_args.cuh -- argument blocks passed by value to the kernels (shared by
+// the translation units of libq3s_sampler.so).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q3s {
+
+struct SampleArgs {
+  int mode, B, V, K;
+  int64_t row_stride;
+  const void* logits;
+  const int64_t* col_shift;
+  const int64_t* token_counts;
+  int64_t tc_stride;
+  const int32_t* history;
+  const int32_t* offsets;
+  int64_t history_len;
+  const float* temperature;
+  float temperature_default;
+  const int32_t* top_k;
+  const float* top_p;
+  float top_p_default;
+  const float* penalty;
+  float penalty_default;
+  const int32_t* min_new;
+  int32_t min_new_default;
+  const int32_t* cur_len;
+  const float* noise;
+  int64_t noise_stride;
+  const float* uniforms;
+  const uint8_t* suppress;
+  int eos_id;
+  int64_t* ids64;
+  int32_t* ids32;
+  int64_t* counts_out;
+  int64_t co_stride;
+  float* processed;
+  int64_t proc_stride;
+  int32_t* row_flags;
+  int32_t* error_word;
+  bool vec_logits;
+  bool vec_counts;
+  bool vec_suppress;
+  bool vec_history;
+};
+
+struct CpArgs {
+  int mode, B, V, S, K, producer;
+  const void* logits;
+  int64_t row_stride, stage_stride;
+  const int64_t* ids_init;
+  const float* temperature;
+  float temperature_default;
+  const float* top_p;
+  float top_p_default;
+  const float* noise;
+  int64_t noise_row_stride, noise_stage_stride;
+  const float* uniforms;
+  int64_t* ids_out;
+  int32_t* row_flags;
+  int32_t* error_word;
+  bool bulk;
+  uint32_t row_bytes;
+  int nbuf;
+};
+
+// Warp-per-row launcher (q3s_warp.cu): icdf steps, 1024 < V <= 3072, V % 8 == 0.
+cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st);
+
+}  // namespace q3s

@@ -3,6 +3,8 @@
 // sample_rows_kernel   one CTA per row: load -> suppress / presence penalty /
 //                      EOS gate -> (greedy | gumbel exactly-K | icdf top-k,
 //                      top-p, inverse-CDF) -> id (+ count update).
+// sample_warp_kernel   one warp per row (q3s_warp.cuh), icdf steps of large
+//                      batches: no block barriers, ~12 rows in flight per SM.
 // cp_frame_kernel      persistent: each CTA walks its rows through all S
 //                      code-predictor stages; stage rows are prefetched into a
 //                      shared-memory ring with cp.async.bulk + mbarrier, and
@@ -23,73 +25,11 @@
 #include <stdio.h>
 #include <string.h>
 
+#include "q3s_args.cuh"
 #include "q3s_device.cuh"
 #include "q3s_sampler.h"
 
 namespace q3s {
-
-// ---------------------------------------------------------------------------
-// argument blocks passed by value to the kernels
-// ---------------------------------------------------------------------------
-
-struct SampleArgs {
-  int mode, B, V, K;
-  int64_t row_stride;
-  const void* logits;
-  const int64_t* col_shift;
-  const int64_t* token_counts;
-  int64_t tc_stride;
-  const int32_t* history;
-  const int32_t* offsets;
-  int64_t history_len;
-  const float* temperature;
-  float temperature_default;
-  const int32_t* top_k;
-  const float* top_p;
-  float top_p_default;
-  const float* penalty;
-  float penalty_default;
-  const int32_t* min_new;
-  int32_t min_new_default;
-  const int32_t* cur_len;
-  const float* noise;
-  int64_t noise_stride;
-  const float* uniforms;
-  const uint8_t* suppress;
-  int eos_id;
-  int64_t* ids64;
-  int32_t* ids32;
-  int64_t* counts_out;
-  int64_t co_stride;
-  float* processed;
-  int64_t proc_stride;
-  int32_t* row_flags;
-  int32_t* error_word;
-  bool vec_logits;
-  bool vec_counts;
-  bool vec_suppress;
-  bool vec_history;
-};
-
-struct CpArgs {
-  int mode, B, V, S, K, producer;
-  const void* logits;
-  int64_t row_stride, stage_stride;
-  const int64_t* ids_init;
-  const float* temperature;
-  float temperature_default;
-  const float* top_p;
-  float top_p_default;
-  const float* noise;
-  int64_t noise_row_stride, noise_stage_stride;
-  const float* uniforms;
-  int64_t* ids_out;
-  int32_t* row_flags;
-  int32_t* error_word;
-  bool bulk;
-  uint32_t row_bytes;
-  int nbuf;
-};
 
 constexpr int MAX_NBUF = 8;
 
@@ -991,39 +931,6 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
 // code-predictor frame: persistent, cp.async.bulk-prefetched stage rows
 // ---------------------------------------------------------------------------
 
-Q3S_DEV void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-Q3S_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-Q3S_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-// Plain (non-multicast) bulk copy global -> this CTA's shared memory.
-Q3S_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-Q3S_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: gives up after ~2^20 polls (each poll itself blocks for a
-// hardware-defined interval) instead of spinning forever.
-Q3S_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (int i = 0; i < (1 << 20); ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-
 template <int NT, int E, bool BF16, int MODE>
 __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
   __shared__ Scratch<NT, E> sh;
@@ -1179,6 +1086,11 @@ q3s_status launch_rows(const q3s::SampleArgs& a, bool bf16, cudaStream_t st) {
   return ok();
 }
 
+// Process-wide kernel policy (q3s_set_kernel_policy).
+int g_policy = Q3S_POLICY_AUTO;
+// Batch size from which AUTO takes warp-per-row.
+constexpr int WARP_MIN_ROWS = 256;
+
 int device_sm_count() {
   static int cache[64] = {0};
   int dev = 0;
@@ -1231,6 +1143,11 @@ extern "C" {
 const char* q3s_last_error_string(void) { return g_last_error; }
 
 int32_t q3s_abi_version(void) { return Q3S_ABI_VERSION; }
+
+int32_t q3s_set_kernel_policy(int32_t policy) {
+  if (policy != Q3S_POLICY_AUTO && policy != Q3S_POLICY_CTA && policy != Q3S_POLICY_WARP) return -1;
+  return __atomic_exchange_n(&g_policy, policy, __ATOMIC_RELAXED);
+}
 
 uint32_t q3s_desc_size(int32_t which) {
   if (which == 0) return static_cast<uint32_t>(sizeof(q3s_sample_desc));
@@ -1330,6 +1247,15 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
   a.vec_history = d->history && aligned16(d->history);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool warp_ok = a.mode == Q3S_DRAW_ICDF && !a.token_counts && !a.col_shift && !a.processed &&
+                       !a.counts_out && V % 8 == 0 && V > 1024 && V <= 3072 && a.vec_logits &&
+                       (!a.suppress || a.vec_suppress);
+  const int policy = __atomic_load_n(&g_policy, __ATOMIC_RELAXED);
+  if (warp_ok && (policy == Q3S_POLICY_WARP || (policy == Q3S_POLICY_AUTO && a.B >= WARP_MIN_ROWS))) {
+    const cudaError_t e = q3s::launch_warp_rows(a, bf16, st);
+    if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample warp launch failed: %s", cudaGetErrorString(e));
+    return ok();
+  }
   if (ne == 16) return launch_rows<512, 16>(a, bf16, st);
   switch (nt) {
     case 64: return launch_rows<64, 8>(a, bf16, st);

@@ -8,11 +8,13 @@ from .ops import (
     CodecSampler,
     CpFramePlan,
     SamplePlan,
+    kernel_policy,
     sample_codebook0,
     sample_cp_frame,
     sample_packed,
     sample_token,
     select_token,
+    set_kernel_policy,
     suppress_mask,
 )
 
@@ -20,11 +22,13 @@ __all__ = [
     "CodecSampler",
     "CpFramePlan",
     "SamplePlan",
+    "kernel_policy",
     "sample_codebook0",
     "sample_cp_frame",
     "sample_packed",
     "sample_token",
     "select_token",
+    "set_kernel_policy",
     "suppress_mask",
     "load_library",
 ]

@@ -22,6 +22,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 DRAW_GUMBEL, DRAW_ICDF = 0, 1
 DTYPE_F32, DTYPE_BF16 = 0, 1
 CP_DIRECT, CP_ROTATE = 0, 1
+POLICY_AUTO, POLICY_CTA, POLICY_WARP = 0, 1, 2
 
 ROW_DRAW_BOUNDARY, ROW_TOPP_BOUNDARY, ROW_GREEDY, ROW_FALLBACK = 1, 2, 4, 8
 DEVERR_HISTORY_ID, DEVERR_OFFSETS, DEVERR_NO_MASS, DEVERR_WAIT_TIMEOUT, DEVERR_CANDIDATES = 1, 2, 4, 8, 16
@@ -107,6 +108,7 @@ EXPORTS = (
     "q3s_last_error_string",
     "q3s_abi_version",
     "q3s_desc_size",
+    "q3s_set_kernel_policy",
 )
 
 _lock = threading.Lock()
@@ -135,6 +137,8 @@ def load(path: str | Path | None = None) -> C.CDLL:
         lib.q3s_abi_version.restype = C.c_int32
         lib.q3s_desc_size.argtypes = [C.c_int32]
         lib.q3s_desc_size.restype = C.c_uint32
+        lib.q3s_set_kernel_policy.argtypes = [C.c_int32]
+        lib.q3s_set_kernel_policy.restype = C.c_int32
         if lib.q3s_abi_version() != Q3S_ABI_VERSION:
             raise RuntimeError(f"q3s ABI {lib.q3s_abi_version()} != binding {Q3S_ABI_VERSION}; rebuild")
         for which, st in ((0, SampleDesc), (1, CpFrameDesc)):

@@ -24,6 +24,7 @@ Errors follow the reference's executor: bad inputs raise ``RuntimeError`` /
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 from dataclasses import dataclass
 from typing import Optional, Sequence, Union
@@ -110,6 +111,27 @@ def _stream_handle(stream: Optional[torch.cuda.Stream]) -> int:
 # ---------------------------------------------------------------------------
 # plans: a filled descriptor plus the tensors it points at
 # ---------------------------------------------------------------------------
+
+def set_kernel_policy(policy: str) -> str:
+    """Choose the kernel family for icdf steps ("auto", "cta" or "warp";
+    process-wide).  Returns the previous policy.  "auto" runs warp-per-row
+    for large batches; both families return the same ids."""
+    codes = {"auto": _lib.POLICY_AUTO, "cta": _lib.POLICY_CTA, "warp": _lib.POLICY_WARP}
+    if policy not in codes:
+        raise ValueError(f"unknown kernel policy {policy!r}")
+    prev = _lib.load().q3s_set_kernel_policy(codes[policy])
+    return {v: k for k, v in codes.items()}[prev]
+
+
+@contextlib.contextmanager
+def kernel_policy(policy: str):
+    """Run a block under a kernel policy, restoring the previous one."""
+    prev = set_kernel_policy(policy)
+    try:
+        yield
+    finally:
+        set_kernel_policy(prev)
+
 
 class SamplePlan:
     """A ready-to-launch ``q3s_sample`` call.

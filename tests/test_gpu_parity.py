@@ -359,3 +359,133 @@ def test_cp_frame_equals_fifteen_single_stage_launches(cuda_device, q3s_lib):
         prev = plan.ids
         outs.append(prev)
     np.testing.assert_array_equal(torch.stack(outs, 1).cpu().numpy(), frame.cpu().numpy())
+
+
+# ---------------------------------------------------------------------------
+# warp-per-row kernels (forced by policy; "auto" picks them for large batches)
+# ---------------------------------------------------------------------------
+
+def _packed_args(b: workloads.Batch, dev):
+    g = b.to(dev)
+    return g, dict(uniforms=g.uniforms, temperature=g.temperature, top_k=g.top_k, top_p=g.top_p,
+                   penalty=g.penalty, min_new_tokens=g.min_new_tokens, suppress=g.suppress, eos_id=g.eos_id)
+
+
+def _run_policy(policy, g, kw, dev):
+    flags = torch.zeros(g.B, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    with q3s.kernel_policy(policy):
+        ids = q3s.sample_packed(g.logits, g.history, g.offsets, row_flags=flags, error_word=err, **kw)
+    torch.cuda.synchronize()
+    return ids.cpu().numpy(), flags.cpu().numpy(), int(err.item())
+
+
+@pytest.mark.parametrize("cfg,rows", [(1, None), (3, None), (4, (0, 1024))])
+def test_warp_kernel_configs_match_oracle_and_cta(cuda_device, q3s_lib, cfg, rows):
+    b = workloads.make_batch(cfg, rows=rows)
+    g, kw = _packed_args(b, cuda_device)
+    ids_w, kf_w, err_w = _run_policy("warp", g, kw, cuda_device)
+    ids_c, kf_c, err_c = _run_policy("cta", g, kw, cuda_device)
+    assert err_w == 0 and err_c == 0
+    ref = oracle_icdf(b)
+    nb, nbm = assert_ids_match(ids_w, ref, kf_w, f"warp config {cfg}", max_frac=MAX_BOUNDARY_FRACTION)
+    # both kernel families agree wherever neither flags a boundary
+    bnd = ((kf_w | kf_c) & (_lib.ROW_DRAW_BOUNDARY | _lib.ROW_TOPP_BOUNDARY)) != 0
+    np.testing.assert_array_equal(ids_w[~bnd], ids_c[~bnd])
+    np.testing.assert_array_equal(kf_w & _lib.ROW_GREEDY, kf_c & _lib.ROW_GREEDY)
+    print(f"warp config {cfg}: {len(ids_w)} rows, {nb} boundary rows, {nbm} differ from the oracle")
+
+
+def _warp_case(dev, logits, bf16=False, **kw):
+    with q3s.kernel_policy("warp"):
+        logits = np.asarray(logits, np.float32)
+        B, V = logits.shape
+        rng = np.random.default_rng(1)
+        u = kw.pop("u", None)
+        u = rng.random(B).astype(np.float32) if u is None else np.asarray(u, np.float32)
+        hist = kw.pop("hist", None) or [np.zeros(0, np.int32)] * B
+        T, k, p = kw.get("T", 1.0), kw.get("k", 0), kw.get("p", 1.0)
+        pen, mn, eos, sup = kw.get("pen", 1.0), kw.get("mn", 0), kw.get("eos", -1), kw.get("suppress")
+        offs = np.zeros(B + 1, np.int32)
+        offs[1:] = np.cumsum([len(h) for h in hist])
+        flat = np.concatenate(hist).astype(np.int32) if offs[-1] else np.zeros(1, np.int32)
+        x_t = torch.from_numpy(logits)
+        if bf16:
+            x_t = x_t.to(torch.bfloat16)
+            logits = x_t.float().numpy()
+        Tv = np.broadcast_to(np.asarray(T, np.float32), (B,)).copy()
+        kv = np.broadcast_to(np.asarray(k, np.int32), (B,)).copy()
+        ref = O.sample_icdf(logits, uniforms=u, temperature=Tv, top_k=kv, top_p=np.full(B, p, np.float32),
+                            penalty=np.full(B, pen, np.float32), history=flat[:offs[-1]], offsets=offs,
+                            min_new_tokens=np.full(B, mn), suppress=sup, eos_id=eos)
+        flags = torch.zeros(B, dtype=torch.int32, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        ids = q3s.sample_packed(x_t.to(dev), _dev(flat, dev), _dev(offs, dev), uniforms=_dev(u, dev),
+                                temperature=_dev(Tv, dev), top_k=_dev(kv, dev), top_p=p, penalty=pen,
+                                min_new_tokens=mn, eos_id=eos, suppress=None if sup is None else _dev(sup, dev),
+                                row_flags=flags, error_word=err)
+        torch.cuda.synchronize()
+        return ids.cpu().numpy(), flags.cpu().numpy(), int(err.item()), ref
+
+
+@pytest.mark.parametrize("V", [1032, 2048, 2056, 3072])
+@pytest.mark.parametrize("k,p", [(0, 1.0), (50, 1.0), (50, 0.9), (0, 0.95), (0, 0.5), (1, 1.0), (300, 0.9)])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_warp_kernel_vocab_sizes_and_filters(cuda_device, q3s_lib, V, k, p, bf16):
+    rng = np.random.default_rng(V * 11 + k)
+    x = (rng.standard_normal((40, V)) * 2.0).astype(np.float32)
+    T = np.where(np.arange(40) % 10 == 3, 0.0, 0.8).astype(np.float32)  # some greedy rows
+    ids, kf, err, ref = _warp_case(cuda_device, x, bf16=bf16, T=T, k=k, p=p)
+    assert err == 0
+    assert_ids_match(ids, ref, kf, f"warp V={V} k={k} p={p} bf16={bf16}", max_frac=0.25)
+
+
+def test_warp_kernel_ties_overflow_and_flat_rows(cuda_device, q3s_lib):
+    x = np.zeros((6, 3072), np.float32)
+    x[0, :100] = 1.0          # 100-way tie across the k=50 boundary: HF keeps all of them
+    x[2, ::3] = -np.inf
+    x[3, :600] = 2.0          # 600-way tie: the candidate list overflows, the exact path runs
+    x[4] = np.linspace(-1, 1, 3072, dtype=np.float32)
+    x[5, 7] = 1e30            # one dominant entry
+    for k, p in ((50, 0.7), (50, 1.0), (0, 0.9), (100, 0.3)):
+        ids, kf, err, ref = _warp_case(cuda_device, x, k=k, p=p)
+        assert err == 0
+        assert_ids_match(ids, ref, kf, f"warp ties k={k} p={p}")
+
+
+def test_warp_kernel_extreme_uniforms_temperatures_and_top_p(cuda_device, q3s_lib):
+    rng = np.random.default_rng(13)
+    x = (rng.standard_normal((8, 3072)) * 3).astype(np.float32)
+    u = np.array([0.0, 0.0, np.float32(1 - 2**-24), np.float32(1 - 2**-24), 0.5, 0.25, 0.75, 0.1], np.float32)
+    ids, kf, _, ref = _warp_case(cuda_device, x, k=0, p=1e-4, u=u)
+    np.testing.assert_array_equal(ids, x.argmax(-1))
+    ids, kf, _, ref = _warp_case(cuda_device, x, k=100, p=1.0, u=u)
+    assert_ids_match(ids, ref, kf, "warp extreme uniforms")
+    # temperatures outside the candidate window take the exact path
+    T = np.array([1e-7, 3e6, 1e-30, 0.5, 2.0, 1e-6, 1e7, 1.0], np.float32)
+    for k, p in ((50, 0.9), (0, 0.9)):
+        ids, kf, err, ref = _warp_case(cuda_device, x, T=T, k=k, p=p, u=u)
+        assert err == 0
+        assert_ids_match(ids, ref, kf, f"warp extreme T k={k}")
+
+
+def test_warp_kernel_penalty_eos_gate_and_suppress(cuda_device, q3s_lib):
+    rng = np.random.default_rng(14)
+    x = (rng.standard_normal((8, 3072)) * 3).astype(np.float32)
+    x[:, 2150] = 50.0
+    hist = [rng.integers(0, 3072, n).astype(np.int32) for n in (0, 1, 5, 9, 30, 64, 65, 4000)]
+    sup = O.suppress_mask(3072, 2150)
+    for k, p in ((50, 0.9), (0, 0.95)):
+        ids, kf, err, ref = _warp_case(cuda_device, x, T=0.9, k=k, p=p, pen=1.3, hist=list(hist), mn=64,
+                                       eos=2150, suppress=sup)
+        assert err == 0
+        assert_ids_match(ids, ref, kf, f"warp penalty/eos k={k}")
+        lens = np.array([len(h) for h in hist])
+        assert np.all(ids[lens < 64] != 2150) and np.all(ids[lens >= 64] == 2150)
+
+
+def test_warp_kernel_bad_history_is_reported(cuda_device, q3s_lib):
+    x = np.zeros((2, 2048), np.float32)
+    hist = [np.array([5, 3000, -1], np.int32), np.array([7], np.int32)]
+    _, _, err, _ = _warp_case(cuda_device, x, hist=hist)
+    assert err & _lib.DEVERR_HISTORY_ID
