@@ -187,9 +187,11 @@ int32_t q3s_abi_version(void);
 uint32_t q3s_desc_size(int32_t which);
 
 /* Kernel family for icdf steps that either family can serve (process-wide;
- * a tuning and test knob with no counterpart in the reference interface).
- * AUTO picks warp-per-row for large batches and CTA-per-row otherwise; the
- * two return the same ids, except that a draw or a top-p cut within 1e-6 of a
+ * a tuning and test knob with no counterpart in the reference interface):
+ * the register-resident CTA-per-row kernel, or the shared-memory-resident
+ * row kernel with W warps per row (W chosen from the batch size, or forced).
+ * AUTO picks the shared-memory kernel for large batches.  All return the
+ * same ids, except that a draw or a top-p cut within 1e-6 of a
  * cumulative-mass edge (flagged in row_flags) may land on either side.
  * Steps that need token_counts, col_shift, processed_logits or counts_out,
  * Gumbel mode, or a vocabulary outside (1024, 3072] or not a multiple of 8
@@ -197,7 +199,11 @@ uint32_t q3s_desc_size(int32_t which);
 typedef enum {
   Q3S_POLICY_AUTO = 0,
   Q3S_POLICY_CTA = 1,
-  Q3S_POLICY_WARP = 2
+  Q3S_POLICY_WARP = 2,   /* shared-memory row kernel, W from the batch size */
+  Q3S_POLICY_ROW_W1 = 3, /* shared-memory row kernel, W forced to 1, 2, 4, 8 */
+  Q3S_POLICY_ROW_W2 = 4,
+  Q3S_POLICY_ROW_W4 = 5,
+  Q3S_POLICY_ROW_W8 = 6
 } q3s_kernel_policy;
 
 /* Set the policy; returns the previous one, or -1 (unchanged) for an unknown

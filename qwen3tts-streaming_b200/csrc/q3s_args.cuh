@@ -66,7 +66,10 @@ struct CpArgs {
   int nbuf;
 };
 
-// Warp-per-row launcher (q3s_warp.cu): icdf steps, 1024 < V <= 3072, V % 8 == 0.
-cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st);
+// Shared-memory row kernels (q3s_warp.cu): icdf steps, 1024 < V <= 3072,
+// V % 8 == 0; `warps` (1, 2, 4 or 8) warps per row.
+cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st, int warps);
+// Warps per row for a batch size on `sm_count` SMs.
+int smem_warps_for(int batch, int sm_count);
 
 }  // namespace q3s

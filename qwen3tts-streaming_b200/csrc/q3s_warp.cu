@@ -1,5 +1,6 @@
-// q3s_warp.cu -- the warp-per-row kernels (q3s_warp.cuh) and their launcher,
-// a translation unit of its own so that it compiles beside q3s_sampler.cu.
+// q3s_warp.cu -- the shared-memory-resident row kernels (q3s_warp.cuh) and
+// their launcher, a translation unit of its own so that it compiles beside
+// q3s_sampler.cu.
 #include <cuda_runtime.h>
 
 #include "q3s_args.cuh"
@@ -8,30 +9,46 @@
 namespace q3s {
 namespace {
 
-template <int R>
-cudaError_t launch_warp(const SampleArgs& a, bool bf16, cudaStream_t st) {
-  constexpr size_t dyn = warp_smem_bytes<R>();
-  auto kern = bf16 ? sample_warp_kernel<R, true> : sample_warp_kernel<R, false>;
-  // more than the 48 KB default of dynamic shared memory: opt in once per
-  // (kernel, device)
-  static bool granted[2][64] = {{false}};
+template <int R, int W>
+cudaError_t launch_smem(const SampleArgs& a, bool bf16, cudaStream_t st) {
+  constexpr size_t dyn = row_smem_bytes<R, W>();
+  auto kern = bf16 ? sample_smem_kernel<R, W, true> : sample_smem_kernel<R, W, false>;
+  // the largest shared-memory carveout, so that ~11 rows fit per SM; set once
+  // per (kernel, device)
+  static bool done[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !granted[bf16 ? 1 : 0][dev]) {
+  if (dev < 0 || dev >= 64 || !done[bf16 ? 1 : 0][dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) granted[bf16 ? 1 : 0][dev] = true;
+    if (dev >= 0 && dev < 64) done[bf16 ? 1 : 0][dev] = true;
   }
-  const int grid = (a.B + WPB - 1) / WPB;
-  kern<<<grid, WPB * 32, dyn, st>>>(a);
+  kern<<<a.B, W * 32, dyn, st>>>(a);
   return cudaGetLastError();
+}
+
+template <int R>
+cudaError_t launch_r(const SampleArgs& a, bool bf16, cudaStream_t st, int w) {
+  switch (w) {
+    case 1: return launch_smem<R, 1>(a, bf16, st);
+    case 2: return launch_smem<R, 2>(a, bf16, st);
+    case 4: return launch_smem<R, 4>(a, bf16, st);
+    default: return launch_smem<R, 8>(a, bf16, st);
+  }
 }
 
 }  // namespace
 
-cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st) {
-  return a.V <= 2048 ? launch_warp<8>(a, bf16, st) : launch_warp<12>(a, bf16, st);
+int smem_warps_for(int batch, int sm_count) {
+  // measured on B200 (V=3072, configs 1/3/4): a row's passes are chains of
+  // dependent shared-memory work, so spreading it over 4 warps beats running
+  // more rows side by side up to B=4096; small batches take 8
+  return batch >= 2 * sm_count ? 4 : 8;
+}
+
+cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st, int warps) {
+  return a.V <= 2048 ? launch_r<8>(a, bf16, st, warps) : launch_r<12>(a, bf16, st, warps);
 }
 
 }  // namespace q3s

@@ -1,13 +1,16 @@
-// q3s_warp.cuh -- warp-per-row sampler (icdf mode) for batched steps.
+// q3s_warp.cuh -- shared-memory-resident row sampler (icdf mode), one CTA of
+// W warps per row (W = 1, 2, 4 or 8, chosen by the batch size).
 //
-// One warp owns one row and keeps it in its own slice of shared memory: the
-// row arrives with one bulk copy (cp.async.bulk, completion on an mbarrier)
-// while the warp scatters the row's history, and every pass over it after
-// that is a rolled loop of 16-byte shared loads -- lane l reads quad
-// h = l + 32 r (entries [4h, 4h+4)) in round r, so a warp's load covers 512
-// contiguous bytes without bank conflicts.  Reductions are warp shuffles; no
-// block barrier is taken, and three CTAs of four warps share an SM.
-// Vocabulary order is quad order: round r, then lane l, then entry j.
+// The row arrives with one bulk copy (cp.async.bulk, completion on an
+// mbarrier) while the CTA scatters the row's history, and stays in shared
+// memory; every pass over it is a rolled loop of 16-byte shared loads --
+// lane l of warp w reads quad h = l + 32 r (entries [4h, 4h+4)) for the
+// rounds r of its block [w RQ/W, (w+1) RQ/W), so a warp's load covers 512
+// contiguous bytes without bank conflicts and each warp's block is a
+// contiguous range of the vocabulary.  Vocabulary order is quad order:
+// round r, then lane l, then entry j.  W = 1 takes no block barrier at all;
+// W > 1 trades barriers for a W-times shorter chain of dependent work per
+// row (small batches are latency-bound, large ones throughput-bound).
 //
 // The arithmetic and the tie rules are those of the CTA-per-row kernels in
 // q3s_sampler.cu (HF LogitsProcessorList order, transformers
@@ -22,33 +25,15 @@
 
 namespace q3s {
 
-constexpr int WPB = 4;                 // warps (rows) per CTA
-constexpr int WCAP = 256;              // candidate records per warp
-constexpr int COARSE_SCALE_BITS = 20;  // coarse masses floor(w * 2^20): a row (V <= 3072, w <= 1) sums below 2^32
+constexpr int WCAP = 256;              // candidate records per row
 constexpr int COARSE_SHIFT = 19;       // coarse bin: exponent and top 4 mantissa bits of w (16 bins per octave)
 constexpr int COARSE_BIN0 = (0x3f800000 >> COARSE_SHIFT) - 255;  // w = 1 -> bin 255; w < 2^-15.9 -> bin 0
-
-template <int R>
-struct alignas(16) WarpSmem {
-  static constexpr int RQ = 2 * R;       // rounds of one quad (4 entries) per lane
-  static constexpr int VMAX = 128 * RQ;  // entries the row buffer holds
-  float4 row[32 * RQ];                   // quad h: logits as loaded -> x' -> s -> softmax weights
-  uint32_t hist[2][NBINS];               // counts / mass high parts, mass low parts; zero between uses
-  union {
-    uint8_t seen[VMAX];                  // presence flags from the packed history (dead after the first pass)
-    uint4 cand[WCAP];                    // candidate records {s bits, index, x' bits, weight bits}
-    float ex[32 * RQ];                   // draw: cumulative weight before each quad
-  } u;
-  uint8_t appb[16 * RQ];                 // presence bits: byte (r/2)*32 + l, nibble r%2 = quad of round r
-  uint8_t keep[WCAP];
-  uint64_t bar;                          // completion of the logits bulk copy
-};
 
 Q3S_DEV int lane_id() { return static_cast<int>(threadIdx.x & 31u); }
 
 // ---------------------------------------------------------------------------
 // warp scans over a 256-bin histogram; each lane owns bins 8l..8l+7 and
-// clears them after reading (the zero invariant of WarpSmem::hist)
+// clears them after reading (the zero invariant of RowSmem::hist)
 // ---------------------------------------------------------------------------
 
 // Bin of the krem-th largest entry (bins descending): returns the bin, its
@@ -140,91 +125,6 @@ Q3S_DEV void warp_scan_mass_asc(uint32_t* hhi, uint32_t* hlo, unsigned long long
   __syncwarp();
 }
 
-// Coarse u32 masses, bins ascending: the first bin where the running sum
-// exceeds tau (tau < total).
-Q3S_DEV uint32_t warp_scan_coarse_asc(uint32_t* hist, uint32_t tau) {
-  const int lane = lane_id();
-  uint4* hb = reinterpret_cast<uint4*>(hist) + 2 * lane;
-  const uint4 a = hb[0], b = hb[1];
-  const uint32_t c[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-  const uint32_t s = (c[0] + c[1]) + (c[2] + c[3]) + (c[4] + c[5]) + (c[6] + c[7]);
-  uint32_t inc = s;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t n = __shfl_up_sync(FULL, inc, o);
-    if (lane >= o) inc += n;
-  }
-  const uint32_t lo0 = inc - s;
-  const bool hit = lo0 <= tau && tau < inc;
-  uint32_t md = 0;
-  if (hit) {
-    uint32_t acc = lo0;
-    bool found = false;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (!found && acc + c[i] > tau) {
-        found = true;
-        md = static_cast<uint32_t>(8 * lane + i);
-      }
-      acc += c[i];
-    }
-  }
-  hb[0] = make_uint4(0, 0, 0, 0);
-  hb[1] = make_uint4(0, 0, 0, 0);
-  const unsigned bal = __ballot_sync(FULL, hit);
-  const uint32_t d = bal ? __shfl_sync(FULL, md, __ffs(bal) - 1) : 255u;
-  __syncwarp();
-  return d;
-}
-
-// Radix select over the row (8-bit digits, most significant first), like
-// select_threshold for a CTA: the k-th largest key, or earlier, once the
-// entries at or above the current bin number at most `stop`, that bin's lower
-// edge.  qk(r, key) fills the keys of this lane's quad of round r and returns
-// the mask of entries that take part.
-template <int RQ, typename QuadKeys>
-Q3S_DEV uint32_t warp_select_rows(uint32_t* hist, int k, int stop, QuadKeys qk) {
-  uint32_t prefix = 0, hmask = 0;
-  uint32_t krem = static_cast<uint32_t>(k);
-#pragma unroll 1
-  for (int shift = 24; shift >= 0; shift -= 8) {
-#pragma unroll 2
-    for (int r = 0; r < RQ; ++r) {
-      uint32_t key[4];
-      const uint32_t act = qk(r, key);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (((act >> j) & 1u) && (key[j] & hmask) == prefix) atomicAdd(&hist[(key[j] >> shift) & 255u], 1u);
-    }
-    __syncwarp();
-    uint32_t d, cnt, knew;
-    warp_scan_count_desc(hist, krem, d, cnt, knew);
-    prefix |= d << shift;
-    hmask |= 255u << shift;
-    krem = knew;
-    // entries strictly above the bin: k - krem (krem = rank left inside it);
-    // in it: cnt
-    if (static_cast<int>(static_cast<uint32_t>(k) - krem + cnt) <= stop) return prefix;
-  }
-  return prefix;
-}
-
-// Radix select of the k-th largest key over a candidate list (positions
-// lane + 32 i); stop as above.
-Q3S_DEV uint32_t warp_select_list(const uint4* cand, int n, uint32_t* hist, int k, int stop) {
-  const int lane = lane_id();
-  return warp_select_rows<WCAP / 128>(hist, k, stop, [&](int r, uint32_t (&key)[4]) -> uint32_t {
-    uint32_t act = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int p = lane + 32 * (4 * r + j);
-      key[j] = p < n ? f2key(__uint_as_float(cand[p].x)) : 0u;
-      act |= (p < n ? 1u : 0u) << j;
-    }
-    return act;
-  });
-}
-
 Q3S_DEV float warp_excl_scan_f(float v, float& total) {
   const int lane = lane_id();
   float inc = v;
@@ -258,117 +158,8 @@ Q3S_DEV unsigned long long warp_sum_u64(unsigned long long v) {
 }
 
 // ---------------------------------------------------------------------------
-// candidate lists (positions in vocabulary order; lane l owns l + 32 q)
+// candidate lists (positions in vocabulary order)
 // ---------------------------------------------------------------------------
-
-// HF TopPLogitsWarper's cut among the participating (keep[i]) entries of a
-// list, given the mass `below0` of everything under the list (every entry
-// below the list is removed, every entry above it kept): an entry is removed
-// when the mass at or below it, in stable ascending order (s asc, index asc),
-// is <= tau.  Requires below0 <= tau < below0 + list mass.  Masses are exact
-// fixed point.  Returns Q3S_ROW_TOPP_BOUNDARY when the cut lies within eps of
-// a cumulative-mass edge.
-Q3S_DEV int warp_mass_cut_list(const uint4* cand, uint8_t* keep, int n, unsigned long long tau,
-                               unsigned long long below0, unsigned long long eps, uint32_t* hhi, uint32_t* hlo) {
-  const int lane = lane_id();
-  constexpr int Q = WCAP / 32;
-  constexpr uint32_t LO = (1u << MASS_LO_BITS) - 1u;
-  uint32_t key[Q];
-  unsigned long long q[Q];
-#pragma unroll
-  for (int i = 0; i < Q; ++i) {
-    const int p = lane + 32 * i;
-    const bool on = p < n && keep[p];
-    key[i] = on ? f2key(__uint_as_float(cand[p].x)) : 0u;
-    q[i] = on ? mass_fixed(__uint_as_float(cand[p].w)) : 0ull;
-  }
-  uint32_t prefix = 0, hmask = 0;
-  unsigned long long below = below0;
-#pragma unroll 1
-  for (int shift = 24; shift >= 0; shift -= 8) {
-#pragma unroll
-    for (int i = 0; i < Q; ++i)
-      if (q[i] != 0 && (key[i] & hmask) == prefix) {
-        const uint32_t bin = (key[i] >> shift) & 255u;
-        atomicAdd(&hhi[bin], static_cast<uint32_t>(q[i] >> MASS_LO_BITS));
-        atomicAdd(&hlo[bin], static_cast<uint32_t>(q[i]) & LO);
-      }
-    __syncwarp();
-    uint32_t d;
-    unsigned long long bef;
-    warp_scan_mass_asc(hhi, hlo, below, tau, d, bef);
-    prefix |= d << shift;
-    hmask |= 255u << shift;
-    below = bef;
-  }
-  const uint32_t vstar = prefix;
-  // all entries at vstar share one s, hence one weight and one mass
-  unsigned long long qs = 0;
-#pragma unroll
-  for (int i = 0; i < Q; ++i)
-    if (q[i] != 0 && key[i] == vstar) qs = q[i];
-  const unsigned bq = __ballot_sync(FULL, qs != 0);
-  qs = __shfl_sync(FULL, qs, bq ? __ffs(bq) - 1 : 0);
-  qs = qs ? qs : 1ull;
-  const unsigned long long nrem = (tau - below) / qs;  // ties removed, lowest index first
-  const unsigned long long first_kept = below + (nrem + 1) * qs;
-  const unsigned long long last_removed = below + nrem * qs;
-  const int flags = ((first_kept - tau) < eps || (tau - last_removed) < eps) ? Q3S_ROW_TOPP_BOUNDARY : 0;
-  unsigned long long ties_before = 0;
-#pragma unroll
-  for (int i = 0; i < Q; ++i) {
-    const int p = lane + 32 * i;
-    const bool on = p < n && keep[p];
-    const bool tie = on && q[i] != 0 && key[i] == vstar;
-    const unsigned bal = __ballot_sync(FULL, tie);
-    const unsigned long long rank = ties_before + __popc(bal & ((1u << lane) - 1u));
-    // zero-mass entries follow their key: kept above vstar, removed at or below
-    const bool kp = on && (key[i] > vstar || (tie && rank >= nrem));
-    ties_before += __popc(bal);
-    if (p < n) keep[p] = kp;
-  }
-  __syncwarp();
-  return flags;
-}
-
-// Keep only the ascending-last participating entry of a list: largest s,
-// then largest index (everything else has mass at or below it <= tau).
-Q3S_DEV void warp_keep_last_list(const uint4* cand, uint8_t* keep, int n) {
-  const int lane = lane_id();
-  constexpr int Q = WCAP / 32;
-  uint32_t bk = 0, bi = 0;
-  int bp = -1;
-#pragma unroll
-  for (int i = 0; i < Q; ++i) {
-    const int p = lane + 32 * i;
-    if (p < n && keep[p]) {
-      const uint32_t k = f2key(__uint_as_float(cand[p].x));
-      if (bp < 0 || k > bk || (k == bk && cand[p].y > bi)) {
-        bk = k;
-        bi = cand[p].y;
-        bp = p;
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    const uint32_t ok = __shfl_xor_sync(FULL, bk, o);
-    const uint32_t oi = __shfl_xor_sync(FULL, bi, o);
-    const int op = __shfl_xor_sync(FULL, bp, o);
-    if (op >= 0 && (bp < 0 || ok > bk || (ok == bk && oi > bi))) {
-      bk = ok;
-      bi = oi;
-      bp = op;
-    }
-  }
-  __syncwarp();
-#pragma unroll
-  for (int i = 0; i < Q; ++i) {
-    const int p = lane + 32 * i;
-    if (p < n) keep[p] = (p == bp);
-  }
-  __syncwarp();
-}
 
 // Inverse CDF over a list's kept weights in vocabulary order: the first
 // position whose running sum exceeds u * total.  Lane l owns positions
@@ -424,69 +215,428 @@ Q3S_DEV int warp_draw_list(const uint4* cand, const uint8_t* keep, int n, float 
   return src * P + rsel;
 }
 
+// Exact fixed-point masses in a coarse histogram (hi/lo parts), bins
+// ascending: the total Zq, tau = floor(frac * Zq), the first bin where the
+// running mass exceeds tau and the mass before it (d = 255, before = Zq when
+// tau >= Zq).  Clears the bins.
+Q3S_DEV void warp_scan_mass_total(uint32_t* hhi, uint32_t* hlo, float frac, unsigned long long& Zq,
+                                  unsigned long long& tau, uint32_t& d, unsigned long long& before) {
+  const int lane = lane_id();
+  uint4* ph = reinterpret_cast<uint4*>(hhi) + 2 * lane;
+  uint4* pl = reinterpret_cast<uint4*>(hlo) + 2 * lane;
+  const uint4 h0 = ph[0], h1 = ph[1], l0 = pl[0], l1 = pl[1];
+  const uint32_t hi[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const uint32_t lo[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  unsigned long long c[8], s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[i] = (static_cast<unsigned long long>(hi[i]) << MASS_LO_BITS) + lo[i];
+    s += c[i];
+  }
+  unsigned long long inc = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long n = __shfl_up_sync(FULL, inc, o);
+    if (lane >= o) inc += n;
+  }
+  Zq = __shfl_sync(FULL, inc, 31);
+  tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
+  const unsigned long long lo0 = inc - s;
+  const bool hit = lo0 <= tau && tau < inc;
+  uint32_t md = 0;
+  unsigned long long mb = 0;
+  if (hit) {
+    unsigned long long acc = lo0;
+    bool found = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (!found && acc + c[i] > tau) {
+        found = true;
+        md = static_cast<uint32_t>(8 * lane + i);
+        mb = acc;
+      }
+      acc += c[i];
+    }
+  }
+  ph[0] = make_uint4(0, 0, 0, 0);
+  ph[1] = make_uint4(0, 0, 0, 0);
+  pl[0] = make_uint4(0, 0, 0, 0);
+  pl[1] = make_uint4(0, 0, 0, 0);
+  const unsigned bal = __ballot_sync(FULL, hit);
+  d = bal ? __shfl_sync(FULL, md, __ffs(bal) - 1) : 255u;
+  before = bal ? __shfl_sync(FULL, mb, __ffs(bal) - 1) : Zq;
+  __syncwarp();
+}
+
 Q3S_DEV uint32_t coarse_bin(float w) {
   const int e = static_cast<int>(__float_as_uint(w) >> COARSE_SHIFT) - COARSE_BIN0;
   return static_cast<uint32_t>(min(255, max(0, e)));
 }
 
 // ---------------------------------------------------------------------------
+// per-row shared memory and the CTA-level steps (W warps share one row)
+// ---------------------------------------------------------------------------
+
+template <int R, int W>
+struct alignas(16) RowSmem {
+  static constexpr int RQ = 2 * R;       // rounds of one quad (4 entries) per lane
+  static constexpr int RPW = RQ / W;     // rounds per warp
+  static constexpr int VMAX = 128 * RQ;  // entries the row buffer holds
+  float4 row[32 * RQ];                   // quad h: logits as loaded -> x' -> s -> softmax weights
+  uint32_t hist[2][NBINS];               // counts / mass high parts, mass low parts; zero between uses
+  union {
+    uint8_t seen[VMAX];                  // presence flags from the packed history (dead after the first pass)
+    uint4 cand[WCAP];                    // candidate records {s bits, index, x' bits, weight bits}
+    float ex[32 * RQ];                   // draw: cumulative weight before each quad, within its warp's block
+  } u;
+  uint8_t appb[32 * RQ];                 // presence bits of quad h (low 4 bits)
+  uint8_t cmask[32 * RQ];                // candidate bits of quad h (low 4 bits)
+  uint8_t keep[WCAP];
+  float xf[2][W];                        // cross-warp exchange, double-buffered
+  int xi[2][W];
+  unsigned long long xq[2][W];
+  uint32_t sel[4];                       // a leader warp's results
+  unsigned long long selq[4];
+  int res[4];
+  uint64_t bar;                          // completion of the logits bulk copy
+};
+
+template <int W>
+Q3S_DEV void row_sync() {
+  if (W == 1)
+    __syncwarp();
+  else
+    __syncthreads();
+}
+
+// CTA-wide exchanges: each takes one barrier (none for W = 1) and combines
+// the per-warp values in warp order, so the results are reproducible.
+template <int R, int W>
+struct RowX {
+  RowSmem<R, W>& sh;
+  int wi, lane, tg = 0;
+  Q3S_DEV float max_f(float v) {
+    v = warp_max_f(v);
+    if (W == 1) return v;
+    if (lane == 0) sh.xf[tg][wi] = v;
+    __syncthreads();
+    float m = sh.xf[tg][0];
+#pragma unroll
+    for (int i = 1; i < W; ++i) m = fmaxf(m, sh.xf[tg][i]);
+    tg ^= 1;
+    return m;
+  }
+  Q3S_DEV float min_f(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(FULL, v, o));
+    if (W == 1) return v;
+    if (lane == 0) sh.xf[tg][wi] = v;
+    __syncthreads();
+    float m = sh.xf[tg][0];
+#pragma unroll
+    for (int i = 1; i < W; ++i) m = fminf(m, sh.xf[tg][i]);
+    tg ^= 1;
+    return m;
+  }
+  Q3S_DEV unsigned long long min_q(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long ov = __shfl_xor_sync(FULL, v, o);
+      v = ov < v ? ov : v;
+    }
+    if (W == 1) return v;
+    if (lane == 0) sh.xq[tg][wi] = v;
+    __syncthreads();
+    unsigned long long m = sh.xq[tg][0];
+#pragma unroll
+    for (int k = 1; k < W; ++k) m = sh.xq[tg][k] < m ? sh.xq[tg][k] : m;
+    tg ^= 1;
+    return m;
+  }
+  Q3S_DEV int max_i(int v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(FULL, v, o));
+    if (W == 1) return v;
+    if (lane == 0) sh.xi[tg][wi] = v;
+    __syncthreads();
+    int m = sh.xi[tg][0];
+#pragma unroll
+    for (int i = 1; i < W; ++i) m = max(m, sh.xi[tg][i]);
+    tg ^= 1;
+    return m;
+  }
+  Q3S_DEV int min_i(int v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(FULL, v, o));
+    if (W == 1) return v;
+    if (lane == 0) sh.xi[tg][wi] = v;
+    __syncthreads();
+    int m = sh.xi[tg][0];
+#pragma unroll
+    for (int i = 1; i < W; ++i) m = min(m, sh.xi[tg][i]);
+    tg ^= 1;
+    return m;
+  }
+  // torch.argmax order over (value, index) pairs
+  Q3S_DEV void argmax(float& v, int& i) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(FULL, v, o);
+      const int oi = __shfl_xor_sync(FULL, i, o);
+      if (arg_better(ov, oi, v, i)) {
+        v = ov;
+        i = oi;
+      }
+    }
+    if (W == 1) return;
+    if (lane == 0) {
+      sh.xf[tg][wi] = v;
+      sh.xi[tg][wi] = i;
+    }
+    __syncthreads();
+    v = sh.xf[tg][0];
+    i = sh.xi[tg][0];
+#pragma unroll
+    for (int k = 1; k < W; ++k)
+      if (arg_better(sh.xf[tg][k], sh.xi[tg][k], v, i)) {
+        v = sh.xf[tg][k];
+        i = sh.xi[tg][k];
+      }
+    tg ^= 1;
+  }
+  // exclusive prefix (warp order) of one uint per warp; total out
+  Q3S_DEV uint32_t prefix_u(uint32_t warp_total, uint32_t& total) {
+    if (W == 1) {
+      total = warp_total;
+      return 0u;
+    }
+    if (lane == 0) sh.xi[tg][wi] = static_cast<int>(warp_total);
+    __syncthreads();
+    uint32_t pre = 0, tot = 0;
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      const uint32_t t = static_cast<uint32_t>(sh.xi[tg][k]);
+      if (k < wi) pre += t;
+      tot += t;
+    }
+    tg ^= 1;
+    total = tot;
+    return pre;
+  }
+  // exclusive prefix (warp order, sequential fp32 adds) of one float per warp
+  Q3S_DEV float prefix_f(float warp_total, float& total) {
+    if (W == 1) {
+      total = warp_total;
+      return 0.0f;
+    }
+    if (lane == 0) sh.xf[tg][wi] = warp_total;
+    __syncthreads();
+    float pre = 0.0f, tot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      if (k == wi) pre = tot;
+      tot = __fadd_rn(tot, sh.xf[tg][k]);
+    }
+    tg ^= 1;
+    total = tot;
+    return pre;
+  }
+  Q3S_DEV unsigned long long max_q(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long ov = __shfl_xor_sync(FULL, v, o);
+      v = ov > v ? ov : v;
+    }
+    if (W == 1) return v;
+    if (lane == 0) sh.xq[tg][wi] = v;
+    __syncthreads();
+    unsigned long long m = sh.xq[tg][0];
+#pragma unroll
+    for (int k = 1; k < W; ++k) m = sh.xq[tg][k] > m ? sh.xq[tg][k] : m;
+    tg ^= 1;
+    return m;
+  }
+  Q3S_DEV unsigned long long sum_q(unsigned long long v) {
+    v = warp_sum_u64(v);
+    if (W == 1) return v;
+    if (lane == 0) sh.xq[tg][wi] = v;
+    __syncthreads();
+    unsigned long long s = 0;
+#pragma unroll
+    for (int k = 0; k < W; ++k) s += sh.xq[tg][k];
+    tg ^= 1;
+    return s;
+  }
+};
+
+// Radix select over the row (8-bit digits, most significant first), like
+// select_threshold for a CTA: the k-th largest key, or earlier, once the
+// entries at or above the current bin number at most `stop`, that bin's lower
+// edge.  Each warp adds its block's keys to the shared histogram (qk(r, key)
+// fills the keys of this lane's quad of round r and returns the mask of
+// entries that take part), warp 0 scans it.
+template <int R, int W, typename QuadKeys>
+Q3S_DEV uint32_t row_select(RowSmem<R, W>& sh, int wi, int k, int stop, QuadKeys qk) {
+  constexpr int RPW = RowSmem<R, W>::RPW;
+  const int lane = lane_id();
+  uint32_t prefix = 0, hmask = 0;
+  uint32_t krem = static_cast<uint32_t>(k);
+#pragma unroll 1
+  for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll 2
+    for (int r = wi * RPW; r < (wi + 1) * RPW; ++r) {
+      uint32_t key[4];
+      const uint32_t act = qk(r, key);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (((act >> j) & 1u) && (key[j] & hmask) == prefix) atomicAdd(&sh.hist[0][(key[j] >> shift) & 255u], 1u);
+    }
+    row_sync<W>();
+    if (wi == 0) {
+      uint32_t d, cnt, knew;
+      warp_scan_count_desc(sh.hist[0], krem, d, cnt, knew);
+      if (lane == 0) {
+        sh.sel[0] = d;
+        sh.sel[1] = cnt;
+        sh.sel[2] = knew;
+      }
+    }
+    row_sync<W>();
+    const uint32_t d = sh.sel[0], cnt = sh.sel[1];
+    krem = sh.sel[2];
+    prefix |= d << shift;
+    hmask |= 255u << shift;
+    // entries strictly above the bin: k - krem (krem = rank left inside it);
+    // in it: cnt
+    if (static_cast<int>(static_cast<uint32_t>(k) - krem + cnt) <= stop) return prefix;
+  }
+  return prefix;
+}
+
+// HF TopPLogitsWarper's cut over a candidate list by all-pairs masses, every
+// thread of the row taking list positions t, t + 32W, ...: an entry of the
+// list (part[p] set) is removed when the exact fixed-point mass at or below
+// it in stable ascending order (s asc, index asc), plus `below0` (the mass of
+// everything under the list, all removed), is <= tau.  cand[p] = {s bits,
+// index, -, weight bits}; n4 = n rounded up to 4 with weightless padding.
+// Writes kept flags to kout[p] and returns Q3S_ROW_TOPP_BOUNDARY when the cut
+// lies within eps of a cumulative-mass edge.  One CTA exchange at the end.
+template <int R, int W>
+Q3S_DEV int row_cut_list(const uint4* cand, const uint8_t* part, uint8_t* kout, int n, int n4,
+                         unsigned long long tau, unsigned long long below0, unsigned long long eps,
+                         RowX<R, W>& X) {
+  const int t = static_cast<int>(threadIdx.x);
+  unsigned long long lr = below0, fk = ~0ull;  // last cum <= tau, first cum > tau
+  for (int p = t; p < n; p += 32 * W) {
+    if (!part[p]) {
+      kout[p] = 0;
+      continue;
+    }
+    const uint4 me = cand[p];
+    const float sp = __uint_as_float(me.x);
+    unsigned long long cum = below0;
+    for (int q = 0; q < n4; q += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 o = cand[q + u];
+        const float so = __uint_as_float(o.x);
+        const bool before = (so < sp) | ((so == sp) & (o.y <= me.y));
+        cum += (before && part[q + u]) ? mass_fixed(__uint_as_float(o.w)) : 0ull;
+      }
+    }
+    const bool kp = cum > tau;
+    kout[p] = kp;
+    if (kp)
+      fk = cum < fk ? cum : fk;
+    else
+      lr = cum > lr ? cum : lr;
+  }
+  lr = X.max_q(lr);
+  fk = X.min_q(fk);
+  return (fk - tau < eps || tau - lr < eps) ? Q3S_ROW_TOPP_BOUNDARY : 0;
+}
+
+// ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 
-template <int R>
-constexpr size_t warp_smem_bytes() {
-  return static_cast<size_t>(WPB) * sizeof(WarpSmem<R>);
+template <int R, int W>
+constexpr size_t row_smem_bytes() {
+  return sizeof(RowSmem<R, W>);
 }
 
-template <int R, bool BF16>
-__global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleArgs a) {
-  extern __shared__ __align__(16) unsigned char q3s_warp_smem[];
-  constexpr int RQ = WarpSmem<R>::RQ;
-  const int wi = static_cast<int>(threadIdx.x >> 5);
-  const int lane = lane_id();
-  const int b = blockIdx.x * WPB + wi;
-  if (b >= a.B) return;  // whole warps leave; no block-wide synchronisation follows
-  WarpSmem<R>& sh = reinterpret_cast<WarpSmem<R>*>(q3s_warp_smem)[wi];
+template <int R, int W, bool BF16>
+__global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a) {
+  extern __shared__ __align__(16) unsigned char q3s_row_smem[];
+  using Smem = RowSmem<R, W>;
+  constexpr int RPW = Smem::RPW;
+  constexpr int NT = 32 * W;
+  Smem& sh = *reinterpret_cast<Smem*>(q3s_row_smem);
+  const int t = static_cast<int>(threadIdx.x);
+  const int wi = t >> 5;
+  const int lane = t & 31;
+  const int b = blockIdx.x;
+  const int rb0 = wi * RPW, rb1 = rb0 + RPW;  // this warp's rounds
   float* rowf = reinterpret_cast<float*>(sh.row);  // entry v at rowf[v]
   const int V = a.V;
   uint32_t err = 0;
+  RowX<R, W> X{sh, wi, lane};
   // fields read inside loops and lambdas, as locals: nothing may take the
   // address of the parameter block (its loads would then stay in the loops)
   const uint8_t* const suppress = a.suppress;
   const int32_t* const history = a.history;
   const int eos_id = a.eos_id;
-
-  // ---- the row's logits stream into shared memory (one bulk copy, no
-  //      multicast) while the history is scattered ---------------------------
   const int esz = BF16 ? 2 : 4;
   const uint32_t row_bytes = static_cast<uint32_t>(V * esz);
-  // bf16 rows land in the upper half of the buffer and are widened in place
-  constexpr uint32_t stage_off = BF16 ? static_cast<uint32_t>(sizeof(sh.row) / 2) : 0u;
   const unsigned char* grow = static_cast<const unsigned char*>(a.logits) + static_cast<int64_t>(b) * a.row_stride * esz;
-  if (lane == 0) {
-    mbar_init(&sh.bar, 1);
-    fence_mbar_init();
-    mbar_expect_tx(&sh.bar, row_bytes);
-    bulk_g2s(reinterpret_cast<unsigned char*>(sh.row) + stage_off, grow, row_bytes, &sh.bar);
-  }
+
+  // ---- first loads: offsets and the suppress words of this warp's quads
+  //      (L2-resident: every row reads them) ---------------------------------
   int o0 = 0, o1 = 0;
   if (history) {
     o0 = __ldg(a.offsets + b);
     o1 = __ldg(a.offsets + b + 1);
   }
+  uint32_t supw[RPW];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int h = lane + 32 * (rb0 + i);
+    supw[i] = (suppress && 4 * h < V) ? __ldg(reinterpret_cast<const uint32_t*>(suppress + 4 * h)) : 0u;
+  }
   {
     // zero the histograms and the presence flags
     uint4* hz = reinterpret_cast<uint4*>(&sh.hist[0][0]);
-#pragma unroll
-    for (int i = 0; i < 2 * NBINS / 4 / 32; ++i) hz[lane + 32 * i] = make_uint4(0, 0, 0, 0);
+    for (int i = t; i < 2 * NBINS / 4; i += NT) hz[i] = make_uint4(0, 0, 0, 0);
     uint4* sz = reinterpret_cast<uint4*>(sh.u.seen);
-#pragma unroll
-    for (int i = 0; i < WarpSmem<R>::VMAX / 16 / 32; ++i) sz[lane + 32 * i] = make_uint4(0, 0, 0, 0);
+    for (int i = t; i < Smem::VMAX / 16; i += NT) sz[i] = make_uint4(0, 0, 0, 0);
   }
-  __syncwarp();
+  row_sync<W>();
 
-  // ---- presence scatter from the packed history (RepetitionPenalty's gather
-  //      set); racing stores of the same byte need no atomics ---------------
+  // ---- the row's logits stream into shared memory (bulk copies, no
+  //      multicast) while the history is scattered.  bf16: warp w's block of
+  //      the row (bytes [256 RPW w, +256 RPW)) lands in the upper half of its
+  //      own fp32 region ([512 RPW w, +512 RPW)), where that warp alone widens
+  //      it in place; fp32 lands as is ------------------------------------------
+  if (t == 0) {
+    mbar_init(&sh.bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&sh.bar, row_bytes);
+    if (BF16) {
+#pragma unroll 1
+      for (int w = 0; w < W; ++w) {
+        const int off = 256 * RPW * w;
+        const int len = min(256 * RPW, static_cast<int>(row_bytes) - off);
+        if (len > 0)
+          bulk_g2s(reinterpret_cast<unsigned char*>(sh.row) + 512 * RPW * w + 256 * RPW, grow + off,
+                   static_cast<uint32_t>(len), &sh.bar);
+      }
+    } else {
+      bulk_g2s(reinterpret_cast<unsigned char*>(sh.row), grow, row_bytes, &sh.bar);
+    }
+  }
+
+  // presence scatter from the packed history (RepetitionPenalty's gather
+  // set); racing stores of the same byte need no atomics
   int hist_len = 0;
   if (history) {
     if (o0 < 0 || o1 < o0 || static_cast<int64_t>(o1) > a.history_len) {
@@ -504,11 +654,11 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
     const int nrest = nhead + (o1 - mid1);
     const int nwork = nrest + (mid1 - mid0) / 4;  // scalar ids first, then 16-byte groups
     constexpr int U = 8;
-    for (int r0 = lane; r0 < nwork; r0 += U * 32) {
+    for (int r0 = t; r0 < nwork; r0 += U * NT) {
       int4 ids[U];
 #pragma unroll
       for (int q = 0; q < U; ++q) {
-        const int rr = r0 + q * 32;
+        const int rr = r0 + q * NT;
         ids[q] = make_int4(-1, -1, -1, -1);
         if (rr < nrest)
           ids[q].x = __ldg(hp + (rr < nhead ? o0 + rr : mid1 + (rr - nhead)));
@@ -517,7 +667,7 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
       }
 #pragma unroll
       for (int q = 0; q < U; ++q) {
-        const int rr = r0 + q * 32;
+        const int rr = r0 + q * NT;
         if (rr >= nwork) continue;
         const int nid = rr < nrest ? 1 : 4;
         const int idv[4] = {ids[q].x, ids[q].y, ids[q].z, ids[q].w};
@@ -531,7 +681,6 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
         }
       }
     }
-    __syncwarp();
   }
   const float T = a.temperature ? __ldg(a.temperature + b) : a.temperature_default;
   const float pen = a.penalty ? __ldg(a.penalty + b) : a.penalty_default;
@@ -553,11 +702,20 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
   const bool cand_path = few && window_ok;
   const bool divT = !greedy && T != 1.0f;  // x / 1 == x exactly
 
-  if (!mbar_wait_bounded(&sh.bar, 0)) {
+  // the presence flags are complete and the mbarrier is initialised; every
+  // thread waits for the row (bounded) and all see the same outcome
+  row_sync<W>();
+  const bool arrived = mbar_wait_bounded(&sh.bar, 0);
+  bool all_arrived;
+  if (W == 1)
+    all_arrived = __all_sync(FULL, arrived);
+  else
+    all_arrived = __syncthreads_and(arrived) != 0;
+  if (!all_arrived) {
     // the copy did not complete in time: report, wait once more (bounded)
     // so that no copy is left writing into a retired CTA's memory, give up
     (void)mbar_wait_bounded(&sh.bar, 0);
-    if (lane == 0) {
+    if (t == 0) {
       if (a.ids64) a.ids64[b] = 0;
       if (a.ids32) a.ids32[b] = 0;
       if (a.row_flags) a.row_flags[b] = Q3S_ROW_FALLBACK;
@@ -566,7 +724,6 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
     return;
   }
 
-  auto app_nib = [&](int r) -> uint32_t { return (sh.appb[(r >> 1) * 32 + lane] >> (4 * (r & 1))) & 15u; };
   // the exact s of entry v: the processors of the first pass and s = x'/T,
   // recomputed from the logits in global memory
   auto exact_s = [&](int v) -> float {
@@ -574,46 +731,32 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
                    : reinterpret_cast<const float*>(grow)[v];
     if (suppress && suppress[v]) x = NEG_SUPPRESS;
     if (gate && v == eos_id) x = -INFINITY;
-    const int h = v >> 2, r = h >> 5, l = h & 31;
-    const uint32_t app = (sh.appb[(r >> 1) * 32 + l] >> (4 * (r & 1) + (v & 3))) & 1u;
-    if (app) x = x > 0.0f ? __fdiv_rn(x, pen) : __fmul_rn(x, pen);
+    if ((sh.appb[v >> 2] >> (v & 3)) & 1u) x = x > 0.0f ? __fdiv_rn(x, pen) : __fmul_rn(x, pen);
     return divT ? __fdiv_rn(x, T) : x;
   };
-  // running maximum of s (and the last index holding it) and torch.argmax of
-  // s (first index) over this lane's entries, vocabulary order
-  float lm = -INFINITY, gv = -INFINITY;
-  int llast = -1, gi = 0x7fffffff;
-  auto track = [&](float s, int v) {
-    if (s > lm) {
-      lm = s;
-      llast = v;
-    } else if (s == lm) {
-      llast = v;
-    }
-    if (arg_better(s, v, gv, gi)) {
-      gv = s;
-      gi = v;
-    }
-  };
+  float lm = -INFINITY, gv = -INFINITY;  // running max of s; torch.argmax of s (greedy rows)
+  int gi = 0x7fffffff;
 
   // ---- first pass: suppress (-1e9, talker_unified_modules.py:409), the EOS
-  //      gate (-inf), the repetition penalty (x * pen for entries <= 0; the
-  //      division of present entries > 0 and the temperature wait for the
-  //      whole-vocabulary path, which does them here) ------------------------
+  //      gate (-inf), the repetition penalty.  Candidate rows defer the
+  //      division of present entries > 0 (x * RN(1/pen) keys select first);
+  //      whole-vocabulary rows compute s = x'/T here.  Branch-free per entry:
+  //      the selects replace data-dependent branches ------------------------
   {
-    const uint2* stg = reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned char*>(sh.row) + stage_off);
-    uint32_t nib = 0;
-#pragma unroll 2
-    for (int r = 0; r < RQ; ++r) {
-      const int h = lane + 32 * r;
+    // this warp's staged bf16 block: local round i at byte 256 i + 8 l
+    const uint2* stg = reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned char*>(sh.row) +
+                                                      512 * RPW * wi + 256 * RPW);
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int h = lane + 32 * (rb0 + i);
       const bool in = 4 * h < V;
       float v[4];
       if (BF16) {
-        // widening in place: round r reads bf16 bytes [stage_off + 256 r,
-        // +256) and writes fp32 bytes [512 r, +512); stage_off = 256 RQ, so
-        // the writes end where the next round's reads begin, at the latest
-        uint2 q = make_uint2(0u, 0u);
-        if (in) q = stg[h];
+        // widening in order within this warp's region: round i reads bf16
+        // bytes [256 RPW + 256 i, +256) and writes fp32 bytes [512 i, +512)
+        // of the region, so the writes end where round i+1's reads begin, at
+        // the latest (i <= RPW - 1)
+        const uint2 q = in ? stg[lane + 32 * i] : make_uint2(0u, 0u);
         __syncwarp();
         v[0] = bf16_bits_to_f32(q.x & 0xffffu);
         v[1] = bf16_bits_to_f32(q.x >> 16);
@@ -626,45 +769,36 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
         v[2] = q.z;
         v[3] = q.w;
       }
-      uint32_t app = 0;
       if (in) {
-        if (suppress) {
-          const uint32_t m4 = __ldg(reinterpret_cast<const uint32_t*>(suppress + 4 * h));
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if ((m4 >> (8 * j)) & 0xffu) v[j] = NEG_SUPPRESS;
-        }
-        if (history) {
-          const uint32_t f = *reinterpret_cast<const uint32_t*>(&sh.u.seen[4 * h]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) app |= (((f >> (8 * j)) & 0xffu) ? 1u : 0u) << j;
-        }
+        const uint32_t f = history ? *reinterpret_cast<const uint32_t*>(&sh.u.seen[4 * h]) : 0u;
+        uint32_t app = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if (gate && 4 * h + j == eos_id) v[j] = -INFINITY;
-          if ((app >> j) & 1u) {
-            if (v[j] > 0.0f) {
-              if (!cand_path) v[j] = __fdiv_rn(v[j], pen);
-            } else {
-              v[j] = __fmul_rn(v[j], pen);
+          const bool ap = ((f >> (8 * j)) & 0xffu) != 0u;
+          app |= (ap ? 1u : 0u) << j;
+          float x = ((supw[i] >> (8 * j)) & 0xffu) ? NEG_SUPPRESS : v[j];
+          x = (gate && 4 * h + j == eos_id) ? -INFINITY : x;
+          if (cand_path) {
+            x = (ap && !(x > 0.0f)) ? __fmul_rn(x, pen) : x;
+          } else {
+            const float dv = __fdiv_rn(x, pen), mv = __fmul_rn(x, pen);
+            x = ap ? (x > 0.0f ? dv : mv) : x;
+            if (divT) x = __fdiv_rn(x, T);
+            lm = fmaxf(lm, x);
+            if (greedy && arg_better(x, 4 * h + j, gv, gi)) {
+              gv = x;
+              gi = 4 * h + j;
             }
           }
-          if (!cand_path) {
-            if (divT) v[j] = __fdiv_rn(v[j], T);
-            track(v[j], 4 * h + j);
-          }
+          v[j] = x;
         }
         sh.row[h] = make_float4(v[0], v[1], v[2], v[3]);
-      }
-      nib |= app << (4 * (r & 1));
-      if (r & 1) {
-        sh.appb[(r >> 1) * 32 + lane] = static_cast<uint8_t>(nib);
-        nib = 0;
+        sh.appb[h] = static_cast<uint8_t>(app);
       }
       if (BF16) __syncwarp();
     }
   }
-  __syncwarp();  // every presence read is done before the union is reused
+  row_sync<W>();  // the row is processed; the presence flags are dead
 
   bool done = false;
   if (cand_path) {
@@ -681,41 +815,44 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
       }
       const float4 q = sh.row[h];
       const float v[4] = {q.x, q.y, q.z, q.w};
-      const uint32_t app = app_nib(r);
+      const uint32_t app = sh.appb[h];
 #pragma unroll
       for (int j = 0; j < 4; ++j) key[j] = f2key((((app >> j) & 1u) && v[j] > 0.0f) ? __fmul_rn(v[j], rpen) : v[j]);
       return 15u;
     };
-    const uint32_t thr = warp_select_rows<RQ>(sh.hist[0], K, WCAP / 2 + K / 2, akeys);
+    const uint32_t thr = row_select<R, W>(sh, wi, K, WCAP / 2 + K / 2, akeys);
     const uint32_t lo = thr > 40u ? thr - 40u : 0u;
-    // candidate records {0, index, x' (not yet divided by pen), 1 if x / pen
-    // is due}, in vocabulary order; two rounds per scan (counts <= 4 each)
-    uint32_t base = 0;
-#pragma unroll 1
-    for (int r = 0; r < RQ; r += 2) {
-      uint32_t key0[4], key1[4];
-      const uint32_t act0 = akeys(r, key0), act1 = akeys(r + 1, key1);
-      uint32_t cm0 = 0, cm1 = 0;
+    // candidates: masks per quad, then records in vocabulary order
+    uint32_t cnt = 0;
+#pragma unroll 2
+    for (int r = rb0; r < rb1; ++r) {
+      uint32_t key[4];
+      const uint32_t act = akeys(r, key);
+      uint32_t cm = 0;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (((act0 >> j) & 1u) && key0[j] >= lo) cm0 |= 1u << j;
-        if (((act1 >> j) & 1u) && key1[j] >= lo) cm1 |= 1u << j;
-      }
-      uint32_t tot;
-      const uint32_t ex = warp_excl_scan_u(__popc(cm0) | (__popc(cm1) << 16), tot);
-      const uint32_t t0 = tot & 0xffffu, t1 = tot >> 16;
-      if (base + t0 + t1 <= static_cast<uint32_t>(WCAP)) {
-        uint32_t p0 = base + (ex & 0xffffu), p1 = base + t0 + (ex >> 16);
+      for (int j = 0; j < 4; ++j)
+        if (((act >> j) & 1u) && key[j] >= lo) cm |= 1u << j;
+      sh.cmask[lane + 32 * r] = static_cast<uint8_t>(cm);
+      cnt += __popc(cm);
+    }
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint32_t cm = q ? cm1 : cm0;
-          if (!cm) continue;
-          const int rr = r + q;
-          const int h = lane + 32 * rr;
+    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
+    uint32_t n32;
+    uint32_t base = X.prefix_u(cnt, n32);
+    const int n = static_cast<int>(n32);
+    const int n4 = (n + 3) & ~3;
+    if (n <= WCAP) {
+      // records {0, index, x' (not yet divided by pen), 1 if x / pen is due}
+#pragma unroll 2
+      for (int r = rb0; r < rb1; ++r) {
+        const int h = lane + 32 * r;
+        const uint32_t cm = sh.cmask[h];
+        uint32_t tot;
+        uint32_t p = base + warp_excl_scan_u(__popc(cm), tot);
+        if (cm) {
           const float4 f = sh.row[h];
           const float v[4] = {f.x, f.y, f.z, f.w};
-          const uint32_t app = app_nib(rr);
-          uint32_t& p = q ? p1 : p0;
+          const uint32_t app = sh.appb[h];
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             if ((cm >> j) & 1u) {
@@ -724,474 +861,517 @@ __global__ void __launch_bounds__(WPB * 32, 3) sample_warp_kernel(const SampleAr
               ++p;
             }
         }
+        base += tot;
       }
-      base += t0 + t1;
     }
-    const int n = static_cast<int>(base);
+    row_sync<W>();
     if (n <= WCAP) {
-      __syncwarp();
-      constexpr int Q = WCAP / 32;
-      // exact x' = x / pen for the flagged candidates
-#pragma unroll 1
-      for (int i = 0; i < Q; ++i) {
-        const int p = lane + 32 * i;
-        if (p < n && sh.u.cand[p].w) {
-          sh.u.cand[p].z = __float_as_uint(__fdiv_rn(__uint_as_float(sh.u.cand[p].z), pen));
-          sh.u.cand[p].w = 0u;
+      // ---- the list, all threads: exact x' and s per candidate (padding
+      //      records never outrank and weigh nothing) --------------------------
+      for (int p = t; p < n4; p += NT) {
+        if (p < n) {
+          const uint4 c = sh.u.cand[p];
+          float x = __uint_as_float(c.z);
+          if (c.w) x = __fdiv_rn(x, pen);
+          const float s = greedy ? x : __fdiv_rn(x, T);
+          sh.u.cand[p] = make_uint4(__float_as_uint(s), c.y, __float_as_uint(x), 0u);
+        } else {
+          sh.u.cand[p] = make_uint4(0xff800000u, 0x7fffffffu, 0xff800000u, 0u);
         }
       }
-      __syncwarp();
+      row_sync<W>();
       if (greedy) {
         // argmax of x' (torch.argmax order: lowest index on ties)
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < Q; ++i) {
-          const int p = lane + 32 * i;
-          if (p < n) {
-            const float xv = __uint_as_float(sh.u.cand[p].z);
-            const int iv = static_cast<int>(sh.u.cand[p].y);
-            if (arg_better(xv, iv, bv, bi)) {
-              bv = xv;
-              bi = iv;
-            }
+        for (int p = t; p < n; p += NT) {
+          const float xv = __uint_as_float(sh.u.cand[p].z);
+          const int iv = static_cast<int>(sh.u.cand[p].y);
+          if (arg_better(xv, iv, bv, bi)) {
+            bv = xv;
+            bi = iv;
           }
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          const float ov = __shfl_xor_sync(FULL, bv, o);
-          const int oi = __shfl_xor_sync(FULL, bi, o);
-          if (arg_better(ov, oi, bv, bi)) {
-            bv = ov;
-            bi = oi;
-          }
-        }
+        X.argmax(bv, bi);
         id = bi;
         flags = Q3S_ROW_GREEDY;
         done = true;
       } else {
-        // s = x'/T; HF TopK keeps s >= the K-th largest s (ties kept)
-        float m = -INFINITY;
-#pragma unroll 1
-        for (int i = 0; i < Q; ++i) {
-          const int p = lane + 32 * i;
-          if (p < n) {
-            const float s = __fdiv_rn(__uint_as_float(sh.u.cand[p].z), T);
-            sh.u.cand[p].x = __float_as_uint(s);
-            m = fmaxf(m, s);
-          }
-        }
-        m = warp_max_f(m);
-        __syncwarp();
-        const uint32_t ks = warp_select_list(sh.u.cand, n, sh.hist[0], K, K);
-        // quotients far from 1 may merge more than 40 key units of x': the
-        // candidate set is proven complete only inside this window
-        const float sk = fabsf(key2f(ks));
-        if (m != -INFINITY && sk >= 0x1p-100f && sk <= 0x1p100f) {
-          unsigned long long lq = 0;
+        // HF TopK keeps s >= the K-th largest s (ties kept): all-pairs ranks;
+        // every rank loop also sees the list's maximum
+        float sk_loc = INFINITY, m_loc = -INFINITY;
+        for (int p = t; p < n; p += NT) {
+          const float sp = __uint_as_float(sh.u.cand[p].x);
+          int above = 0;
+          float m = -INFINITY;
+          for (int q = 0; q < n4; q += 4) {
 #pragma unroll
-          for (int i = 0; i < Q; ++i) {
-            const int p = lane + 32 * i;
-            if (p < n) {
-              const float s = __uint_as_float(sh.u.cand[p].x);
-              const bool sv = f2key(s) >= ks;
-              const float wgt = sv ? softmax_weight(s, m) : 0.0f;
-              sh.keep[p] = sv;
-              sh.u.cand[p].w = __float_as_uint(wgt);
-              lq += sv ? mass_fixed(wgt) : 0ull;
+            for (int v = 0; v < 4; ++v) {
+              const float so = __uint_as_float(sh.u.cand[q + v].x);
+              above += so > sp;
+              m = fmaxf(m, so);
             }
           }
-          __syncwarp();
+          const bool sv = above < K;
+          sh.keep[p] = sv;
+          sh.u.cand[p].w = __float_as_uint(sv ? softmax_weight(sp, m) : 0.0f);
+          if (sv) sk_loc = fminf(sk_loc, sp);
+          m_loc = m;
+        }
+        for (int p = n + t; p < n4; p += NT) sh.keep[p] = 0;
+        const float sk = fabsf(X.min_f(sk_loc));
+        const float mm = X.max_f(m_loc);
+        row_sync<W>();
+        // quotients far from 1 may merge more than 40 key units of x': the
+        // candidate set is proven complete only inside this window
+        if (mm != -INFINITY && sk >= 0x1p-100f && sk <= 0x1p100f) {
+          uint8_t* kout = sh.cmask;  // kept entries
           if (top_p < 1.0f) {
-            const unsigned long long Zq = warp_sum_u64(lq);
+            unsigned long long lq = 0;
+            for (int p = t; p < n; p += NT)
+              if (sh.keep[p]) lq += mass_fixed(__uint_as_float(sh.u.cand[p].w));
+            const unsigned long long Zq = X.sum_q(lq);
             const float frac = __fsub_rn(1.0f, top_p);
             const unsigned long long tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
-            if (tau >= Zq)
-              warp_keep_last_list(sh.u.cand, sh.keep, n);
-            else
-              flags |= warp_mass_cut_list(sh.u.cand, sh.keep, n, tau, 0ull, Zq / 1000000ull, sh.hist[0], sh.hist[1]);
+            if (tau >= Zq) {
+              // only the ascending-last survivor stays: largest s, then index
+              unsigned long long best = 0;
+              for (int p = t; p < n; p += NT)
+                if (sh.keep[p]) {
+                  const unsigned long long key = (static_cast<unsigned long long>(f2key(__uint_as_float(
+                                                      sh.u.cand[p].x))) << 32) | sh.u.cand[p].y;
+                  best = key > best ? key : best;
+                }
+              best = X.max_q(best);
+              for (int p = t; p < n; p += NT)
+                kout[p] = sh.keep[p] && sh.u.cand[p].y == static_cast<uint32_t>(best & 0xffffffffu);
+            } else {
+              flags |= row_cut_list<R, W>(sh.u.cand, sh.keep, kout, n, n4, tau, 0ull, Zq / 1000000ull, X);
+            }
+          } else {
+            for (int p = t; p < n; p += NT) kout[p] = sh.keep[p];
           }
-          const int pos = warp_draw_list(sh.u.cand, sh.keep, n, u, flags);
-          id = static_cast<int>(sh.u.cand[pos].y);
+          row_sync<W>();
+          if (wi == 0) {
+            int lflags = 0;
+            const int pos = warp_draw_list(sh.u.cand, kout, n, u, lflags);
+            if (lane == 0) {
+              sh.res[0] = static_cast<int>(sh.u.cand[pos].y);
+              sh.res[1] = lflags;
+            }
+          }
+          row_sync<W>();
+          id = sh.res[0];
+          flags |= sh.res[1];
           done = true;
         }
       }
-      __syncwarp();
     }
     if (!done) {
-      // the candidate set overflowed or left the proven window: finish s for
+      // the candidate set overflowed or left the proven window: exact s for
       // the whole row in place
 #pragma unroll 2
-      for (int r = 0; r < RQ; ++r) {
+      for (int r = rb0; r < rb1; ++r) {
         const int h = lane + 32 * r;
         if (4 * h >= V) continue;
         const float4 f = sh.row[h];
         float v[4] = {f.x, f.y, f.z, f.w};
-        const uint32_t app = app_nib(r);
+        const uint32_t app = sh.appb[h];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if (((app >> j) & 1u) && v[j] > 0.0f) v[j] = __fdiv_rn(v[j], pen);
-          if (divT) v[j] = __fdiv_rn(v[j], T);
-          track(v[j], 4 * h + j);
+          float x = v[j];
+          const float dv = __fdiv_rn(x, pen);
+          x = (((app >> j) & 1u) && x > 0.0f) ? dv : x;
+          if (divT) x = __fdiv_rn(x, T);
+          lm = fmaxf(lm, x);
+          if (greedy && arg_better(x, 4 * h + j, gv, gi)) {
+            gv = x;
+            gi = 4 * h + j;
+          }
+          v[j] = x;
         }
         sh.row[h] = make_float4(v[0], v[1], v[2], v[3]);
       }
-      __syncwarp();
+      flags = 0;
+      row_sync<W>();
     }
   }
-
   if (!done) {
     // ---- whole-vocabulary rows: the row holds s -------------------------
     flags = 0;
-    const float m = warp_max_f(lm);
     if (greedy) {
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(FULL, gv, o);
-        const int oi = __shfl_xor_sync(FULL, gi, o);
-        if (arg_better(ov, oi, gv, gi)) {
-          gv = ov;
-          gi = oi;
-        }
-      }
+      X.argmax(gv, gi);
       id = gi;
       flags = Q3S_ROW_GREEDY;
-    } else if (m == -INFINITY) {
-      // nothing finite: report it and take the lowest index
-      err |= Q3S_DEVERR_NO_MASS;
-      flags = Q3S_ROW_FALLBACK;
-      id = 0;
     } else {
-      // the ascending-last entry: largest s, then largest index (it survives
-      // top-k, which keeps ties at the top)
-      int last = lm == m ? llast : -1;
+      const float m = X.max_f(lm);
+      if (m == -INFINITY) {
+        // nothing finite: report it and take the lowest index
+        err |= Q3S_DEVERR_NO_MASS;
+        flags = Q3S_ROW_FALLBACK;
+        id = 0;
+      } else {
+        // top-k survivors: s >= the k-th largest s (ties kept)
+        const bool topk = kk > 0 && kk < V;
+        uint32_t kth = 0;
+        if (topk) {
+          kth = row_select<R, W>(sh, wi, kk, kk, [&](int r, uint32_t (&key)[4]) -> uint32_t {
+            const int h = lane + 32 * r;
+            if (4 * h >= V) {
 #pragma unroll
-      for (int o = 16; o; o >>= 1) last = max(last, __shfl_xor_sync(FULL, last, o));
-      // top-k survivors: s >= the k-th largest s (ties kept)
-      const bool topk = kk > 0 && kk < V;
-      uint32_t kth = 0;
-      if (topk) {
-        kth = warp_select_rows<RQ>(sh.hist[0], kk, kk, [&](int r, uint32_t (&key)[4]) -> uint32_t {
-          const int h = lane + 32 * r;
-          if (4 * h >= V) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) key[j] = 0u;
-            return 0u;
-          }
-          const float4 f = sh.row[h];
-          key[0] = f2key(f.x);
-          key[1] = f2key(f.y);
-          key[2] = f2key(f.z);
-          key[3] = f2key(f.w);
-          return 15u;
-        });
-      }
-      // ---- softmax weights in place; exact total mass; coarse histogram of
-      //      approximate masses by the weight's exponent and top 4 mantissa
-      //      bits (monotone in s) ----------------------------------------------
-      const bool cut = top_p < 1.0f;
-      unsigned long long lq = 0;
-      uint32_t lc = 0;
-#pragma unroll 2
-      for (int r = 0; r < RQ; ++r) {
-        const int h = lane + 32 * r;
-        if (4 * h >= V) continue;
-        const float4 f = sh.row[h];
-        const float sv[4] = {f.x, f.y, f.z, f.w};
-        float wv[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const bool surv = !topk || f2key(sv[j]) >= kth;
-          wv[j] = surv ? softmax_weight(sv[j], m) : 0.0f;
-          if (cut && wv[j] > 0.0f) {
-            lq += mass_fixed(wv[j]);
-            const uint32_t c = __float2uint_rd(__fmul_rn(wv[j], static_cast<float>(1u << COARSE_SCALE_BITS)));
-            lc += c;
-            if (c) atomicAdd(&sh.hist[0][coarse_bin(wv[j])], c);
-          }
+              for (int j = 0; j < 4; ++j) key[j] = 0u;
+              return 0u;
+            }
+            const float4 f = sh.row[h];
+            key[0] = f2key(f.x);
+            key[1] = f2key(f.y);
+            key[2] = f2key(f.z);
+            key[3] = f2key(f.w);
+            return 15u;
+          });
         }
-        sh.row[h] = make_float4(wv[0], wv[1], wv[2], wv[3]);
-      }
-      __syncwarp();
-      uint32_t blo = 0;  // the draw counts weights in coarse bins >= blo
-      bool single = false;
-      if (cut) {
-        const unsigned long long Zq = warp_sum_u64(lq);
-        const float frac = __fsub_rn(1.0f, top_p);
-        const unsigned long long tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
-        const unsigned long long eps = Zq / 1000000ull;
-        uint32_t Zc = lc;
+        // ---- softmax weights in place; exact fixed-point masses into a
+        //      coarse histogram by the weight's exponent and top 4 mantissa
+        //      bits (monotone in s) ------------------------------------------
+        const bool cut = top_p < 1.0f;
+        constexpr uint32_t LO = (1u << MASS_LO_BITS) - 1u;
+#pragma unroll 2
+        for (int r = rb0; r < rb1; ++r) {
+          const int h = lane + 32 * r;
+          if (4 * h >= V) continue;
+          const float4 f = sh.row[h];
+          const float sv[4] = {f.x, f.y, f.z, f.w};
+          float wv[4];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) Zc += __shfl_xor_sync(FULL, Zc, o);
-        const uint32_t tau_c = min(__double2uint_rd(static_cast<double>(frac) * static_cast<double>(Zc)),
-                                   Zc > 0 ? Zc - 1 : 0u);
-        const uint32_t bstar = warp_scan_coarse_asc(sh.hist[0], tau_c);
-        if (tau >= Zq) {
-          // everything but the ascending-last entry goes
-          id = last;
-          single = true;
-        } else {
-          // exact masses below and inside the coarse window [wlo, whi];
-          // window entries become candidate records in vocabulary order
-          const uint32_t wlo = bstar > 0 ? bstar - 1 : 0u;
-          const uint32_t whi = bstar < 255 ? bstar + 1 : 255u;
-          unsigned long long lb = 0, lw = 0;
-          uint32_t base = 0;
-#pragma unroll 1
-          for (int r = 0; r < RQ; r += 2) {
-            uint32_t cm[2] = {0u, 0u};
-            float wq[2][4];
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const int h = lane + 32 * (r + q);
-              const float4 f = (4 * h < V) ? sh.row[h] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-              wq[q][0] = f.x;
-              wq[q][1] = f.y;
-              wq[q][2] = f.z;
-              wq[q][3] = f.w;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float w1 = wq[q][j];
-                if (w1 > 0.0f) {
-                  const uint32_t bn = coarse_bin(w1);
-                  const unsigned long long q1 = mass_fixed(w1);
-                  if (bn < wlo) {
-                    lb += q1;
-                  } else if (bn <= whi) {
-                    lw += q1;
-                    cm[q] |= 1u << j;
-                  }
-                }
+          for (int j = 0; j < 4; ++j) {
+            const bool surv = !topk || f2key(sv[j]) >= kth;
+            wv[j] = surv ? softmax_weight(sv[j], m) : 0.0f;
+            if (cut) {
+              const unsigned long long q = mass_fixed(wv[j]);
+              if (q) {
+                const uint32_t bn = coarse_bin(wv[j]);
+                atomicAdd(&sh.hist[0][bn], static_cast<uint32_t>(q >> MASS_LO_BITS));
+                atomicAdd(&sh.hist[1][bn], static_cast<uint32_t>(q) & LO);
               }
             }
-            uint32_t tot;
-            const uint32_t ex = warp_excl_scan_u(__popc(cm[0]) | (__popc(cm[1]) << 16), tot);
-            const uint32_t t0 = tot & 0xffffu, t1 = tot >> 16;
-            if (base + t0 + t1 <= static_cast<uint32_t>(WCAP)) {
-#pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                uint32_t p = base + (q ? t0 + (ex >> 16) : (ex & 0xffffu));
-                const int h = lane + 32 * (r + q);
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  if ((cm[q] >> j) & 1u) {
-                    sh.u.cand[p] = make_uint4(0u, static_cast<uint32_t>(4 * h + j), 0u, __float_as_uint(wq[q][j]));
-                    sh.keep[p] = 1;
-                    ++p;
-                  }
-              }
-            }
-            base += t0 + t1;
           }
-          const unsigned long long below = warp_sum_u64(lb);
-          const unsigned long long wmass = warp_sum_u64(lw);
-          const int n = static_cast<int>(base);
-          __syncwarp();
-          if (below <= tau && tau < below + wmass && n <= WCAP) {
-            // the cut lies inside the window: exact s of its entries, the
-            // exact cut, and removed entries' weights zeroed in the row
-#pragma unroll 1
-            for (int i = 0; i < WCAP / 32; ++i) {
-              const int p = lane + 32 * i;
-              if (p < n) sh.u.cand[p].x = __float_as_uint(exact_s(static_cast<int>(sh.u.cand[p].y)));
+          sh.row[h] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+        }
+        row_sync<W>();
+        bool single = false;
+        if (cut) {
+          const float frac = __fsub_rn(1.0f, top_p);
+          if (wi == 0) {
+            unsigned long long Zq, tau, before;
+            uint32_t bstar;
+            warp_scan_mass_total(sh.hist[0], sh.hist[1], frac, Zq, tau, bstar, before);
+            if (lane == 0) {
+              sh.selq[0] = Zq;
+              sh.selq[1] = tau;
+              sh.selq[2] = before;
+              sh.sel[3] = bstar;
             }
-            __syncwarp();
-            flags |= warp_mass_cut_list(sh.u.cand, sh.keep, n, tau, below, eps, sh.hist[0], sh.hist[1]);
+          }
+          row_sync<W>();
+          const unsigned long long Zq = sh.selq[0], tau = sh.selq[1], below = sh.selq[2];
+          const uint32_t bstar = sh.sel[3];
+          const unsigned long long eps = Zq / 1000000ull;
+          if (tau >= Zq) {
+            // everything but the ascending-last entry (largest s, then largest
+            // index) goes; its weight is exp(0) = 1
+            int last = -1;
 #pragma unroll 1
-            for (int i = 0; i < WCAP / 32; ++i) {
-              const int p = lane + 32 * i;
-              if (p < n && !sh.keep[p]) rowf[sh.u.cand[p].y] = 0.0f;
-            }
-            blo = wlo;
-          } else {
-            // the coarse window missed (approximate masses) or holds too many
-            // entries: an exact radix cut over every survivor, keys from the
-            // exact s recomputed per entry
-            auto skey = [&](int v) -> uint32_t { return f2key(exact_s(v)); };
-            uint32_t prefix = 0, hmask = 0;
-            unsigned long long bl = 0;
-            constexpr uint32_t LO = (1u << MASS_LO_BITS) - 1u;
-#pragma unroll 1
-            for (int shift = 24; shift >= 0; shift -= 8) {
-#pragma unroll 1
-              for (int r = 0; r < RQ; ++r) {
-                const int h = lane + 32 * r;
-                if (4 * h >= V) continue;
-                const float4 f = sh.row[h];
-                const float wv[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const unsigned long long q1 = mass_fixed(wv[j]);
-                  if (q1 == 0) continue;
-                  const uint32_t key = skey(4 * h + j);
-                  if ((key & hmask) == prefix) {
-                    atomicAdd(&sh.hist[0][(key >> shift) & 255u], static_cast<uint32_t>(q1 >> MASS_LO_BITS));
-                    atomicAdd(&sh.hist[1][(key >> shift) & 255u], static_cast<uint32_t>(q1) & LO);
-                  }
-                }
-              }
-              __syncwarp();
-              uint32_t d;
-              unsigned long long bef;
-              warp_scan_mass_asc(sh.hist[0], sh.hist[1], bl, tau, d, bef);
-              prefix |= d << shift;
-              hmask |= 255u << shift;
-              bl = bef;
-            }
-            const uint32_t vstar = prefix;
-            // the entries at vstar share one s, one weight and one mass
-            unsigned long long qs = 0;
-#pragma unroll 1
-            for (int r = 0; r < RQ; ++r) {
+            for (int r = rb0; r < rb1; ++r) {
               const int h = lane + 32 * r;
               if (4 * h >= V) continue;
               const float4 f = sh.row[h];
               const float wv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
               for (int j = 0; j < 4; ++j)
-                if (mass_fixed(wv[j]) != 0 && skey(4 * h + j) == vstar) qs = mass_fixed(wv[j]);
+                if (wv[j] == 1.0f && exact_s(4 * h + j) == m) last = 4 * h + j;
             }
-            const unsigned bq = __ballot_sync(FULL, qs != 0);
-            qs = __shfl_sync(FULL, qs, bq ? __ffs(bq) - 1 : 0);
-            qs = qs ? qs : 1ull;
-            const unsigned long long nrem = (tau - bl) / qs;  // ties removed, lowest index first
-            const unsigned long long first_kept = bl + (nrem + 1) * qs;
-            const unsigned long long last_removed = bl + nrem * qs;
-            if ((first_kept - tau) < eps || (tau - last_removed) < eps) flags |= Q3S_ROW_TOPP_BOUNDARY;
-            unsigned long long tb = 0;  // ties in earlier rounds
-#pragma unroll 1
-            for (int r = 0; r < RQ; ++r) {
+            id = X.max_i(last);
+            single = true;
+          } else {
+            // entries below the crossing bin go (their weights are zeroed),
+            // entries above it stay; the crossing bin's entries are resolved
+            // exactly as a list
+            uint32_t cnt = 0;
+#pragma unroll 2
+            for (int r = rb0; r < rb1; ++r) {
               const int h = lane + 32 * r;
-              const bool in = 4 * h < V;
-              float wv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-              uint32_t key[4] = {0u, 0u, 0u, 0u};
-              uint32_t ce = 0;
-              if (in) {
+              uint32_t cm = 0;
+              if (4 * h < V) {
                 const float4 f = sh.row[h];
-                wv[0] = f.x;
-                wv[1] = f.y;
-                wv[2] = f.z;
-                wv[3] = f.w;
+                float wv[4] = {f.x, f.y, f.z, f.w};
+                bool zeroed = false;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                  key[j] = wv[j] > 0.0f ? skey(4 * h + j) : 0u;
-                  if (mass_fixed(wv[j]) != 0 && key[j] == vstar) ce |= 1u << j;
-                }
-              }
-              uint32_t tot;
-              uint32_t t_in = warp_excl_scan_u(__popc(ce), tot);
-              if (in) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  bool kp = false;
                   if (wv[j] > 0.0f) {
+                    const uint32_t bn = coarse_bin(wv[j]);
+                    if (bn < bstar) {
+                      wv[j] = 0.0f;
+                      zeroed = true;
+                    } else if (bn == bstar) {
+                      cm |= 1u << j;
+                    }
+                  }
+                }
+                if (zeroed) sh.row[h] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+              }
+              sh.cmask[h] = static_cast<uint8_t>(cm);
+              cnt += __popc(cm);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
+            uint32_t n32;
+            uint32_t base = X.prefix_u(cnt, n32);
+            const int n = static_cast<int>(n32);
+            if (n <= WCAP) {
+#pragma unroll 2
+              for (int r = rb0; r < rb1; ++r) {
+                const int h = lane + 32 * r;
+                const uint32_t cm = sh.cmask[h];
+                uint32_t tot;
+                uint32_t p = base + warp_excl_scan_u(__popc(cm), tot);
+                if (cm) {
+                  const float4 f = sh.row[h];
+                  const float wv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                  for (int j = 0; j < 4; ++j)
+                    if ((cm >> j) & 1u) {
+                      sh.u.cand[p] = make_uint4(0u, static_cast<uint32_t>(4 * h + j), 0u, __float_as_uint(wv[j]));
+                      sh.keep[p] = 1;
+                      ++p;
+                    }
+                }
+                base += tot;
+              }
+              row_sync<W>();
+              // exact s of the crossing bin's entries, the exact cut over
+              // them, and the removed entries' weights zeroed in the row
+              const int n4 = (n + 3) & ~3;
+              for (int p = t; p < n4; p += NT) {
+                if (p < n)
+                  sh.u.cand[p].x = __float_as_uint(exact_s(static_cast<int>(sh.u.cand[p].y)));
+                else
+                  sh.u.cand[p] = make_uint4(0xff800000u, 0x7fffffffu, 0u, 0u);
+                sh.keep[p] = p < n;
+              }
+              row_sync<W>();
+              uint8_t* kout = sh.cmask;
+              flags |= row_cut_list<R, W>(sh.u.cand, sh.keep, kout, n, n4, tau, below, eps, X);
+              for (int p = t; p < n; p += NT)
+                if (!kout[p]) rowf[sh.u.cand[p].y] = 0.0f;
+              row_sync<W>();
+            } else {
+              // the crossing bin holds too many entries: an exact radix cut
+              // over the survivors of that bin and above, keys from the exact
+              // s recomputed per entry
+              auto skey = [&](int v) -> uint32_t { return f2key(exact_s(v)); };
+              uint32_t prefix = 0, hmask = 0;
+              unsigned long long bl = below;
+#pragma unroll 1
+              for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll 1
+                for (int r = rb0; r < rb1; ++r) {
+                  const int h = lane + 32 * r;
+                  if (4 * h >= V) continue;
+                  const float4 f = sh.row[h];
+                  const float wv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const unsigned long long q1 = mass_fixed(wv[j]);
+                    if (q1 == 0 || coarse_bin(wv[j]) != bstar) continue;
+                    const uint32_t key = skey(4 * h + j);
+                    if ((key & hmask) == prefix) {
+                      atomicAdd(&sh.hist[0][(key >> shift) & 255u], static_cast<uint32_t>(q1 >> MASS_LO_BITS));
+                      atomicAdd(&sh.hist[1][(key >> shift) & 255u], static_cast<uint32_t>(q1) & LO);
+                    }
+                  }
+                }
+                row_sync<W>();
+                if (wi == 0) {
+                  uint32_t d;
+                  unsigned long long bef;
+                  warp_scan_mass_asc(sh.hist[0], sh.hist[1], bl, tau, d, bef);
+                  if (lane == 0) {
+                    sh.sel[0] = d;
+                    sh.selq[3] = bef;
+                  }
+                }
+                row_sync<W>();
+                prefix |= sh.sel[0] << shift;
+                hmask |= 255u << shift;
+                bl = sh.selq[3];
+              }
+              const uint32_t vstar = prefix;
+              // the entries at vstar share one s, one weight and one mass
+              unsigned long long qs = 0;
+#pragma unroll 1
+              for (int r = rb0; r < rb1; ++r) {
+                const int h = lane + 32 * r;
+                if (4 * h >= V) continue;
+                const float4 f = sh.row[h];
+                const float wv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  if (mass_fixed(wv[j]) != 0 && coarse_bin(wv[j]) == bstar && skey(4 * h + j) == vstar)
+                    qs = mass_fixed(wv[j]);
+              }
+              qs = X.max_q(qs);
+              qs = qs ? qs : 1ull;
+              const unsigned long long nrem = (tau - bl) / qs;  // ties removed, lowest index first
+              const unsigned long long first_kept = bl + (nrem + 1) * qs;
+              const unsigned long long last_removed = bl + nrem * qs;
+              if ((first_kept - tau) < eps || (tau - last_removed) < eps) flags |= Q3S_ROW_TOPP_BOUNDARY;
+              // tie ranks in vocabulary order: per-round warp scans, warp
+              // blocks offset by the earlier warps' tie counts
+              uint32_t tcount = 0;
+#pragma unroll 1
+              for (int r = rb0; r < rb1; ++r) {
+                const int h = lane + 32 * r;
+                if (4 * h >= V) continue;
+                const float4 f = sh.row[h];
+                const float wv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  if (mass_fixed(wv[j]) != 0 && coarse_bin(wv[j]) == bstar && skey(4 * h + j) == vstar) ++tcount;
+              }
+#pragma unroll
+              for (int o = 16; o; o >>= 1) tcount += __shfl_xor_sync(FULL, tcount, o);
+              uint32_t ttot;
+              unsigned long long tb = X.prefix_u(tcount, ttot);
+#pragma unroll 1
+              for (int r = rb0; r < rb1; ++r) {
+                const int h = lane + 32 * r;
+                const bool in = 4 * h < V;
+                float wv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                uint32_t key[4] = {0u, 0u, 0u, 0u};
+                uint32_t ce = 0, inb = 0;
+                if (in) {
+                  const float4 f = sh.row[h];
+                  wv[0] = f.x;
+                  wv[1] = f.y;
+                  wv[2] = f.z;
+                  wv[3] = f.w;
+#pragma unroll
+                  for (int j = 0; j < 4; ++j)
+                    if (wv[j] > 0.0f && coarse_bin(wv[j]) == bstar) {
+                      inb |= 1u << j;
+                      key[j] = skey(4 * h + j);
+                      if (mass_fixed(wv[j]) != 0 && key[j] == vstar) ce |= 1u << j;
+                    }
+                }
+                uint32_t tot;
+                uint32_t t_in = warp_excl_scan_u(__popc(ce), tot);
+                if (in && inb) {
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    if (!((inb >> j) & 1u)) continue;
+                    bool kp = false;
                     if (key[j] > vstar) {
                       kp = true;
                     } else if ((ce >> j) & 1u) {
                       kp = tb + t_in >= nrem;
                       ++t_in;
                     }
+                    if (!kp) wv[j] = 0.0f;
                   }
-                  if (!kp) wv[j] = 0.0f;
+                  sh.row[h] = make_float4(wv[0], wv[1], wv[2], wv[3]);
                 }
-                sh.row[h] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+                tb += tot;
               }
-              tb += tot;
-            }
-            blo = 0;
-          }
-          __syncwarp();
-        }
-      }
-      if (!single) {
-        // ---- inverse CDF in vocabulary order: cumulative weight before each
-        //      quad (round scans), then the first quad whose running sum
-        //      passes u * total, then the entry inside it -------------------
-        float carry = 0.0f;
-        int lastv = -1;
-#pragma unroll 1
-        for (int r = 0; r < RQ; ++r) {
-          const int h = lane + 32 * r;
-          float qsum = 0.0f;
-          if (4 * h < V) {
-            const float4 f = sh.row[h];
-            const float wv[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float w1 = (wv[j] > 0.0f && coarse_bin(wv[j]) >= blo) ? wv[j] : 0.0f;
-              qsum = __fadd_rn(qsum, w1);
-              if (w1 > 0.0f) lastv = 4 * h + j;
+              row_sync<W>();
             }
           }
-          float tot;
-          const float exs = warp_excl_scan_f(qsum, tot);
-          sh.u.ex[r * 32 + lane] = __fadd_rn(carry, exs);
-          carry = __fadd_rn(carry, tot);
         }
-        __syncwarp();
-        const float W = carry;
-        const float thr = __fmul_rn(u, W);
-        // this lane's first quad (vocabulary order) whose running sum > thr
-        int firstq = 0x7fffffff;
+        if (!single) {
+          // ---- inverse CDF in vocabulary order: cumulative weight before each
+          //      quad (round scans within each warp's block, warp blocks in
+          //      order), the first quad whose running sum passes u * total,
+          //      then the entry inside it --------------------------------------
+          float carry = 0.0f;
+          int lastv = -1;
 #pragma unroll 1
-        for (int r = 0; r < RQ; ++r) {
-          const int h = lane + 32 * r;
-          if (4 * h >= V) break;
-          const float4 f = sh.row[h];
-          const float wv[4] = {f.x, f.y, f.z, f.w};
-          float acc = sh.u.ex[r * 32 + lane];
-          bool hit = false;
+          for (int r = rb0; r < rb1; ++r) {
+            const int h = lane + 32 * r;
+            float qsum = 0.0f;
+            if (4 * h < V) {
+              const float4 f = sh.row[h];
+              const float wv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float w1 = (wv[j] > 0.0f && coarse_bin(wv[j]) >= blo) ? wv[j] : 0.0f;
-            acc = __fadd_rn(acc, w1);
-            hit |= w1 > 0.0f && acc > thr;
-          }
-          if (hit) {
-            firstq = r * 32 + lane;
-            break;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          firstq = min(firstq, __shfl_xor_sync(FULL, firstq, o));
-          lastv = max(lastv, __shfl_xor_sync(FULL, lastv, o));
-        }
-        if (firstq == 0x7fffffff) {
-          id = lastv;
-          flags |= Q3S_ROW_FALLBACK;
-        } else {
-          const int ol = firstq & 31, orr = firstq >> 5;
-          int pick = 0, near = 0;
-          if (lane == ol) {
-            const int h = lane + 32 * orr;
-            const float4 f = sh.row[h];
-            const float wv[4] = {f.x, f.y, f.z, f.w};
-            const float pre = sh.u.ex[orr * 32 + lane];
-            float acc = pre, prev = pre, cdf = pre;
-            bool found = false;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float w1 = (wv[j] > 0.0f && coarse_bin(wv[j]) >= blo) ? wv[j] : 0.0f;
-              const float before = acc;
-              acc = __fadd_rn(acc, w1);
-              if (!found && w1 > 0.0f && acc > thr) {
-                found = true;
-                pick = 4 * h + j;
-                prev = before;
-                cdf = acc;
+              for (int j = 0; j < 4; ++j) {
+                qsum = __fadd_rn(qsum, wv[j]);
+                if (wv[j] > 0.0f) lastv = 4 * h + j;
               }
             }
-            const float tol = BOUNDARY_EPS * W;
-            near = (__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol);
+            float tot;
+            const float exs = warp_excl_scan_f(qsum, tot);
+            sh.u.ex[h] = __fadd_rn(carry, exs);
+            carry = __fadd_rn(carry, tot);
           }
-          id = __shfl_sync(FULL, pick, ol);
-          if (__shfl_sync(FULL, near, ol)) flags |= Q3S_ROW_DRAW_BOUNDARY;
+          float Wt;
+          const float off = X.prefix_f(carry, Wt);
+          const float thr = __fmul_rn(u, Wt);
+          int firstq = 0x7fffffff;
+#pragma unroll 1
+          for (int r = rb0; r < rb1; ++r) {
+            const int h = lane + 32 * r;
+            if (4 * h >= V) break;
+            const float4 f = sh.row[h];
+            const float wv[4] = {f.x, f.y, f.z, f.w};
+            float acc = __fadd_rn(off, sh.u.ex[h]);
+            bool hit = false;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              acc = __fadd_rn(acc, wv[j]);
+              hit |= wv[j] > 0.0f && acc > thr;
+            }
+            if (hit) {
+              firstq = h;
+              break;
+            }
+          }
+          // quads in vocabulary order are h = l + 32 r ascending
+          firstq = X.min_i(firstq);
+          lastv = X.max_i(lastv);
+          if (firstq == 0x7fffffff) {
+            id = lastv;
+            flags |= Q3S_ROW_FALLBACK;
+          } else {
+            const int ow = (firstq >> 5) / RPW;
+            if (wi == ow && lane == (firstq & 31)) {
+              const float4 f = sh.row[firstq];
+              const float wv[4] = {f.x, f.y, f.z, f.w};
+              const float pre = __fadd_rn(off, sh.u.ex[firstq]);
+              float acc = pre, prev = pre, cdf = pre;
+              int pick = 4 * firstq;
+              bool found = false;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float before = acc;
+                acc = __fadd_rn(acc, wv[j]);
+                if (!found && wv[j] > 0.0f && acc > thr) {
+                  found = true;
+                  pick = 4 * firstq + j;
+                  prev = before;
+                  cdf = acc;
+                }
+              }
+              const float tol = BOUNDARY_EPS * Wt;
+              sh.res[0] = pick;
+              sh.res[1] = ((__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol)) ? Q3S_ROW_DRAW_BOUNDARY : 0;
+            }
+            row_sync<W>();
+            id = sh.res[0];
+            flags |= sh.res[1];
+          }
         }
       }
     }
   }
-  if (lane == 0) {
+  if (t == 0) {
     if (a.ids64) a.ids64[b] = id;
     if (a.ids32) a.ids32[b] = id;
     if (a.row_flags) a.row_flags[b] = flags;

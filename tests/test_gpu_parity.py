@@ -21,6 +21,8 @@ pytestmark = pytest.mark.gpu
 
 RTOL = 1e-5
 MAX_BOUNDARY_FRACTION = 0.02
+# the shared-memory row kernel with 1, 2, 4 and 8 warps per row
+WARP_POLICIES = ["w1", "w2", "w4", "w8"]
 
 
 def _dev(x, dev):
@@ -380,11 +382,12 @@ def _run_policy(policy, g, kw, dev):
     return ids.cpu().numpy(), flags.cpu().numpy(), int(err.item())
 
 
+@pytest.mark.parametrize("policy", ["warp"] + WARP_POLICIES)
 @pytest.mark.parametrize("cfg,rows", [(1, None), (3, None), (4, (0, 1024))])
-def test_warp_kernel_configs_match_oracle_and_cta(cuda_device, q3s_lib, cfg, rows):
+def test_warp_kernel_configs_match_oracle_and_cta(cuda_device, q3s_lib, cfg, rows, policy):
     b = workloads.make_batch(cfg, rows=rows)
     g, kw = _packed_args(b, cuda_device)
-    ids_w, kf_w, err_w = _run_policy("warp", g, kw, cuda_device)
+    ids_w, kf_w, err_w = _run_policy(policy, g, kw, cuda_device)
     ids_c, kf_c, err_c = _run_policy("cta", g, kw, cuda_device)
     assert err_w == 0 and err_c == 0
     ref = oracle_icdf(b)
@@ -396,8 +399,8 @@ def test_warp_kernel_configs_match_oracle_and_cta(cuda_device, q3s_lib, cfg, row
     print(f"warp config {cfg}: {len(ids_w)} rows, {nb} boundary rows, {nbm} differ from the oracle")
 
 
-def _warp_case(dev, logits, bf16=False, **kw):
-    with q3s.kernel_policy("warp"):
+def _warp_case(dev, logits, bf16=False, policy="warp", **kw):
+    with q3s.kernel_policy(policy):
         logits = np.asarray(logits, np.float32)
         B, V = logits.shape
         rng = np.random.default_rng(1)
@@ -431,16 +434,18 @@ def _warp_case(dev, logits, bf16=False, **kw):
 @pytest.mark.parametrize("V", [1032, 2048, 2056, 3072])
 @pytest.mark.parametrize("k,p", [(0, 1.0), (50, 1.0), (50, 0.9), (0, 0.95), (0, 0.5), (1, 1.0), (300, 0.9)])
 @pytest.mark.parametrize("bf16", [False, True])
-def test_warp_kernel_vocab_sizes_and_filters(cuda_device, q3s_lib, V, k, p, bf16):
+@pytest.mark.parametrize("policy", WARP_POLICIES)
+def test_warp_kernel_vocab_sizes_and_filters(cuda_device, q3s_lib, V, k, p, bf16, policy):
     rng = np.random.default_rng(V * 11 + k)
     x = (rng.standard_normal((40, V)) * 2.0).astype(np.float32)
     T = np.where(np.arange(40) % 10 == 3, 0.0, 0.8).astype(np.float32)  # some greedy rows
-    ids, kf, err, ref = _warp_case(cuda_device, x, bf16=bf16, T=T, k=k, p=p)
+    ids, kf, err, ref = _warp_case(cuda_device, x, bf16=bf16, policy=policy, T=T, k=k, p=p)
     assert err == 0
-    assert_ids_match(ids, ref, kf, f"warp V={V} k={k} p={p} bf16={bf16}", max_frac=0.25)
+    assert_ids_match(ids, ref, kf, f"{policy} V={V} k={k} p={p} bf16={bf16}", max_frac=0.25)
 
 
-def test_warp_kernel_ties_overflow_and_flat_rows(cuda_device, q3s_lib):
+@pytest.mark.parametrize("policy", WARP_POLICIES)
+def test_warp_kernel_ties_overflow_and_flat_rows(cuda_device, q3s_lib, policy):
     x = np.zeros((6, 3072), np.float32)
     x[0, :100] = 1.0          # 100-way tie across the k=50 boundary: HF keeps all of them
     x[2, ::3] = -np.inf
@@ -448,44 +453,47 @@ def test_warp_kernel_ties_overflow_and_flat_rows(cuda_device, q3s_lib):
     x[4] = np.linspace(-1, 1, 3072, dtype=np.float32)
     x[5, 7] = 1e30            # one dominant entry
     for k, p in ((50, 0.7), (50, 1.0), (0, 0.9), (100, 0.3)):
-        ids, kf, err, ref = _warp_case(cuda_device, x, k=k, p=p)
+        ids, kf, err, ref = _warp_case(cuda_device, x, policy=policy, k=k, p=p)
         assert err == 0
-        assert_ids_match(ids, ref, kf, f"warp ties k={k} p={p}")
+        assert_ids_match(ids, ref, kf, f"{policy} ties k={k} p={p}")
 
 
-def test_warp_kernel_extreme_uniforms_temperatures_and_top_p(cuda_device, q3s_lib):
+@pytest.mark.parametrize("policy", WARP_POLICIES)
+def test_warp_kernel_extreme_uniforms_temperatures_and_top_p(cuda_device, q3s_lib, policy):
     rng = np.random.default_rng(13)
     x = (rng.standard_normal((8, 3072)) * 3).astype(np.float32)
     u = np.array([0.0, 0.0, np.float32(1 - 2**-24), np.float32(1 - 2**-24), 0.5, 0.25, 0.75, 0.1], np.float32)
-    ids, kf, _, ref = _warp_case(cuda_device, x, k=0, p=1e-4, u=u)
+    ids, kf, _, ref = _warp_case(cuda_device, x, policy=policy, k=0, p=1e-4, u=u)
     np.testing.assert_array_equal(ids, x.argmax(-1))
-    ids, kf, _, ref = _warp_case(cuda_device, x, k=100, p=1.0, u=u)
+    ids, kf, _, ref = _warp_case(cuda_device, x, policy=policy, k=100, p=1.0, u=u)
     assert_ids_match(ids, ref, kf, "warp extreme uniforms")
     # temperatures outside the candidate window take the exact path
     T = np.array([1e-7, 3e6, 1e-30, 0.5, 2.0, 1e-6, 1e7, 1.0], np.float32)
     for k, p in ((50, 0.9), (0, 0.9)):
-        ids, kf, err, ref = _warp_case(cuda_device, x, T=T, k=k, p=p, u=u)
+        ids, kf, err, ref = _warp_case(cuda_device, x, policy=policy, T=T, k=k, p=p, u=u)
         assert err == 0
         assert_ids_match(ids, ref, kf, f"warp extreme T k={k}")
 
 
-def test_warp_kernel_penalty_eos_gate_and_suppress(cuda_device, q3s_lib):
+@pytest.mark.parametrize("policy", WARP_POLICIES)
+def test_warp_kernel_penalty_eos_gate_and_suppress(cuda_device, q3s_lib, policy):
     rng = np.random.default_rng(14)
     x = (rng.standard_normal((8, 3072)) * 3).astype(np.float32)
     x[:, 2150] = 50.0
     hist = [rng.integers(0, 3072, n).astype(np.int32) for n in (0, 1, 5, 9, 30, 64, 65, 4000)]
     sup = O.suppress_mask(3072, 2150)
     for k, p in ((50, 0.9), (0, 0.95)):
-        ids, kf, err, ref = _warp_case(cuda_device, x, T=0.9, k=k, p=p, pen=1.3, hist=list(hist), mn=64,
-                                       eos=2150, suppress=sup)
+        ids, kf, err, ref = _warp_case(cuda_device, x, policy=policy, T=0.9, k=k, p=p, pen=1.3, hist=list(hist),
+                                       mn=64, eos=2150, suppress=sup)
         assert err == 0
         assert_ids_match(ids, ref, kf, f"warp penalty/eos k={k}")
         lens = np.array([len(h) for h in hist])
         assert np.all(ids[lens < 64] != 2150) and np.all(ids[lens >= 64] == 2150)
 
 
-def test_warp_kernel_bad_history_is_reported(cuda_device, q3s_lib):
+@pytest.mark.parametrize("policy", WARP_POLICIES)
+def test_warp_kernel_bad_history_is_reported(cuda_device, q3s_lib, policy):
     x = np.zeros((2, 2048), np.float32)
     hist = [np.array([5, 3000, -1], np.int32), np.array([7], np.int32)]
-    _, _, err, _ = _warp_case(cuda_device, x, hist=hist)
+    _, _, err, _ = _warp_case(cuda_device, x, policy=policy, hist=hist)
     assert err & _lib.DEVERR_HISTORY_ID
