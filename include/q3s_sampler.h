@@ -203,7 +203,8 @@ typedef enum {
   Q3S_POLICY_ROW_W1 = 3, /* shared-memory row kernel, W forced to 1, 2, 4, 8 */
   Q3S_POLICY_ROW_W2 = 4,
   Q3S_POLICY_ROW_W4 = 5,
-  Q3S_POLICY_ROW_W8 = 6
+  Q3S_POLICY_ROW_W8 = 6,
+  Q3S_POLICY_ROW_WMAX = 7 /* W = 12 (V > 2048) or 16 (V <= 2048) */
 } q3s_kernel_policy;
 
 /* Set the policy; returns the previous one, or -1 (unchanged) for an unknown

@@ -1145,7 +1145,7 @@ const char* q3s_last_error_string(void) { return g_last_error; }
 int32_t q3s_abi_version(void) { return Q3S_ABI_VERSION; }
 
 int32_t q3s_set_kernel_policy(int32_t policy) {
-  if (policy < Q3S_POLICY_AUTO || policy > Q3S_POLICY_ROW_W8) return -1;
+  if (policy < Q3S_POLICY_AUTO || policy > Q3S_POLICY_ROW_WMAX) return -1;
   return __atomic_exchange_n(&g_policy, policy, __ATOMIC_RELAXED);
 }
 
@@ -1257,6 +1257,7 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
     if (policy == Q3S_POLICY_ROW_W2) warps = 2;
     if (policy == Q3S_POLICY_ROW_W4) warps = 4;
     if (policy == Q3S_POLICY_ROW_W8) warps = 8;
+    if (policy == Q3S_POLICY_ROW_WMAX) warps = 0;
     const cudaError_t e = q3s::launch_warp_rows(a, bf16, st, warps);
     if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample warp launch failed: %s", cudaGetErrorString(e));
     return ok();

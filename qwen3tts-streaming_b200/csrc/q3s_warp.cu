@@ -30,11 +30,15 @@ cudaError_t launch_smem(const SampleArgs& a, bool bf16, cudaStream_t st) {
 
 template <int R>
 cudaError_t launch_r(const SampleArgs& a, bool bf16, cudaStream_t st, int w) {
+  // the widest variant splits the rows' rounds (2R) into 2 per warp (R = 12)
+  // or 1 per warp (R = 8)
+  constexpr int WMAX = R == 12 ? 12 : 16;
   switch (w) {
     case 1: return launch_smem<R, 1>(a, bf16, st);
     case 2: return launch_smem<R, 2>(a, bf16, st);
     case 4: return launch_smem<R, 4>(a, bf16, st);
-    default: return launch_smem<R, 8>(a, bf16, st);
+    case 8: return launch_smem<R, 8>(a, bf16, st);
+    default: return launch_smem<R, WMAX>(a, bf16, st);
   }
 }
 

@@ -164,23 +164,21 @@ Q3S_DEV unsigned long long warp_sum_u64(unsigned long long v) {
 // Inverse CDF over a list's kept weights in vocabulary order: the first
 // position whose running sum exceeds u * total.  Lane l owns positions
 // [l P, l P + P), P = ceil(n / 32) -- the association order of the CTA
-// kernels' warp-0 finisher, so both produce the same sums.
-Q3S_DEV int warp_draw_list(const uint4* cand, const uint8_t* keep, int n, float u, int& flags) {
+// kernels' warp-0 finisher, so both produce the same sums.  The weight of
+// position p = l P + r is wk[r * 32 + l] (transposed: conflict-free loads),
+// 0 for removed entries and for p >= n.
+Q3S_DEV int warp_draw_list(const float* wk, int n, float u, int& flags) {
   const int lane = lane_id();
   const int P = (n + 31) / 32;
   float a = 0.0f;
-  for (int r = 0; r < P; ++r) {
-    const int i = lane * P + r;
-    if (i < n && keep[i]) a = __fadd_rn(a, __uint_as_float(cand[i].w));
-  }
+  for (int r = 0; r < P; ++r) a = __fadd_rn(a, wk[r * 32 + lane]);
   float W;
   const float pre = warp_excl_scan_f(a, W);
   const float thr = __fmul_rn(u, W);
   int r_first = -1, r_last = -1;
   float acc = 0.0f;
   for (int r = 0; r < P; ++r) {
-    const int i = lane * P + r;
-    const float w = (i < n && keep[i]) ? __uint_as_float(cand[i].w) : 0.0f;
+    const float w = wk[r * 32 + lane];
     acc = __fadd_rn(acc, w);
     if (w > 0.0f) {
       r_last = r;
@@ -202,9 +200,7 @@ Q3S_DEV int warp_draw_list(const uint4* cand, const uint8_t* keep, int n, float 
   if (lane == src) {
     float cdf = pre, prev = pre, a2 = 0.0f;
     for (int r = 0; r <= rsel; ++r) {
-      const int i = lane * P + r;
-      const float w = (i < n && keep[i]) ? __uint_as_float(cand[i].w) : 0.0f;
-      a2 = __fadd_rn(a2, w);
+      a2 = __fadd_rn(a2, wk[r * 32 + lane]);
       if (r < rsel) prev = __fadd_rn(pre, a2);
       cdf = __fadd_rn(pre, a2);
     }
@@ -213,6 +209,15 @@ Q3S_DEV int warp_draw_list(const uint4* cand, const uint8_t* keep, int n, float 
   }
   if (__shfl_sync(FULL, near, src)) flags |= Q3S_ROW_DRAW_BOUNDARY;
   return src * P + rsel;
+}
+
+// Exclusive prefix over the lanes of a small count (0..7) and the warp total,
+// from three ballots.
+Q3S_DEV uint32_t warp_excl_small(uint32_t c, uint32_t& total) {
+  const uint32_t lt = (1u << lane_id()) - 1u;
+  const unsigned b0 = __ballot_sync(FULL, c & 1u), b1 = __ballot_sync(FULL, c & 2u), b2 = __ballot_sync(FULL, c & 4u);
+  total = __popc(b0) + 2u * __popc(b1) + 4u * __popc(b2);
+  return __popc(b0 & lt) + 2u * __popc(b1 & lt) + 4u * __popc(b2 & lt);
 }
 
 // Exact fixed-point masses in a coarse histogram (hi/lo parts), bins
@@ -268,6 +273,14 @@ Q3S_DEV void warp_scan_mass_total(uint32_t* hhi, uint32_t* hlo, float frac, unsi
   __syncwarp();
 }
 
+// Bin of an entry d >= 0 below the row's largest approximate value, bins of
+// width 1/scale from d0 on: floor((d - d0) * scale), 255 from 255/scale on
+// (entries above d0 -- d < d0 -- are not binned).  Monotone in d.
+Q3S_DEV uint32_t top_bin(float d, float d0, float scale) {
+  const float e = __fmul_rn(__fsub_rn(d, d0), scale);
+  return e < 255.0f ? static_cast<uint32_t>(e) : 255u;
+}
+
 Q3S_DEV uint32_t coarse_bin(float w) {
   const int e = static_cast<int>(__float_as_uint(w) >> COARSE_SHIFT) - COARSE_BIN0;
   return static_cast<uint32_t>(min(255, max(0, e)));
@@ -293,8 +306,10 @@ struct alignas(16) RowSmem {
   uint8_t cmask[32 * RQ];                // candidate bits of quad h (low 4 bits)
   uint8_t keep[WCAP];
   float xf[2][W];                        // cross-warp exchange, double-buffered
+  float xf2[2][W];
   int xi[2][W];
   unsigned long long xq[2][W];
+  unsigned long long xq2[2][W];
   uint32_t sel[4];                       // a leader warp's results
   unsigned long long selq[4];
   int res[4];
@@ -456,6 +471,50 @@ struct RowX {
     tg ^= 1;
     return m;
   }
+  // two maxima in one exchange
+  Q3S_DEV void max2_q(unsigned long long& a0, unsigned long long& a1) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long o0 = __shfl_xor_sync(FULL, a0, o), o1 = __shfl_xor_sync(FULL, a1, o);
+      a0 = o0 > a0 ? o0 : a0;
+      a1 = o1 > a1 ? o1 : a1;
+    }
+    if (W == 1) return;
+    if (lane == 0) {
+      sh.xq[tg][wi] = a0;
+      sh.xq2[tg][wi] = a1;
+    }
+    __syncthreads();
+    a0 = sh.xq[tg][0];
+    a1 = sh.xq2[tg][0];
+#pragma unroll
+    for (int k = 1; k < W; ++k) {
+      a0 = sh.xq[tg][k] > a0 ? sh.xq[tg][k] : a0;
+      a1 = sh.xq2[tg][k] > a1 ? sh.xq2[tg][k] : a1;
+    }
+    tg ^= 1;
+  }
+  Q3S_DEV void max2_f(float& a0, float& a1) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      a0 = fmaxf(a0, __shfl_xor_sync(FULL, a0, o));
+      a1 = fmaxf(a1, __shfl_xor_sync(FULL, a1, o));
+    }
+    if (W == 1) return;
+    if (lane == 0) {
+      sh.xf[tg][wi] = a0;
+      sh.xf2[tg][wi] = a1;
+    }
+    __syncthreads();
+    a0 = sh.xf[tg][0];
+    a1 = sh.xf2[tg][0];
+#pragma unroll
+    for (int k = 1; k < W; ++k) {
+      a0 = fmaxf(a0, sh.xf[tg][k]);
+      a1 = fmaxf(a1, sh.xf2[tg][k]);
+    }
+    tg ^= 1;
+  }
   Q3S_DEV unsigned long long sum_q(unsigned long long v) {
     v = warp_sum_u64(v);
     if (W == 1) return v;
@@ -518,15 +577,15 @@ Q3S_DEV uint32_t row_select(RowSmem<R, W>& sh, int wi, int k, int stop, QuadKeys
 // list (part[p] set) is removed when the exact fixed-point mass at or below
 // it in stable ascending order (s asc, index asc), plus `below0` (the mass of
 // everything under the list, all removed), is <= tau.  cand[p] = {s bits,
-// index, -, weight bits}; n4 = n rounded up to 4 with weightless padding.
-// Writes kept flags to kout[p] and returns Q3S_ROW_TOPP_BOUNDARY when the cut
-// lies within eps of a cumulative-mass edge.  One CTA exchange at the end.
-template <int R, int W>
-Q3S_DEV int row_cut_list(const uint4* cand, const uint8_t* part, uint8_t* kout, int n, int n4,
-                         unsigned long long tau, unsigned long long below0, unsigned long long eps,
-                         RowX<R, W>& X) {
+// index, -, -}; mq[q] = the mass of participant q (0 for others and for the
+// padding up to n4).  Writes kept flags to kout[p]; ORs Q3S_ROW_TOPP_BOUNDARY
+// into *flag_word when a cumulative mass (or below0) lies within eps of tau.
+template <int W>
+Q3S_DEV void row_cut_list(const uint4* cand, const uint8_t* part, const unsigned long long* mq, uint8_t* kout,
+                          int n, int n4, unsigned long long tau, unsigned long long below0, unsigned long long eps,
+                          int* flag_word) {
   const int t = static_cast<int>(threadIdx.x);
-  unsigned long long lr = below0, fk = ~0ull;  // last cum <= tau, first cum > tau
+  bool near = t == 0 && tau - below0 < eps;
   for (int p = t; p < n; p += 32 * W) {
     if (!part[p]) {
       kout[p] = 0;
@@ -537,23 +596,40 @@ Q3S_DEV int row_cut_list(const uint4* cand, const uint8_t* part, uint8_t* kout, 
     unsigned long long cum = below0;
     for (int q = 0; q < n4; q += 4) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint4 o = cand[q + u];
+      for (int v = 0; v < 4; ++v) {
+        const uint4 o = cand[q + v];
         const float so = __uint_as_float(o.x);
         const bool before = (so < sp) | ((so == sp) & (o.y <= me.y));
-        cum += (before && part[q + u]) ? mass_fixed(__uint_as_float(o.w)) : 0ull;
+        cum += before ? mq[q + v] : 0ull;
       }
     }
     const bool kp = cum > tau;
     kout[p] = kp;
-    if (kp)
-      fk = cum < fk ? cum : fk;
-    else
-      lr = cum > lr ? cum : lr;
+    near |= kp ? (cum - tau < eps) : (tau - cum < eps);
   }
-  lr = X.max_q(lr);
-  fk = X.min_q(fk);
-  return (fk - tau < eps || tau - lr < eps) ? Q3S_ROW_TOPP_BOUNDARY : 0;
+  if (near) atomicOr(flag_word, Q3S_ROW_TOPP_BOUNDARY);
+}
+
+// Kept weights of a list into the draw's transposed layout (positions
+// p < 32 ceil(n/32)), then the draw in warp 0.  Returns the chosen position
+// in every thread (through res[0]) and ORs the draw's flags into res[1].
+template <int R, int W>
+Q3S_DEV int row_draw_list(RowSmem<R, W>& sh, const uint8_t* kout, float* wk, int n, float u) {
+  const int t = static_cast<int>(threadIdx.x);
+  const int P = (n + 31) / 32;
+  for (int p = t; p < 32 * P; p += 32 * W)
+    wk[(p % P) * 32 + p / P] = (p < n && kout[p]) ? __uint_as_float(sh.u.cand[p].w) : 0.0f;
+  row_sync<W>();
+  if (t < 32) {
+    int lflags = 0;
+    const int pos = warp_draw_list(wk, n, u, lflags);
+    if (t == 0) {
+      sh.res[0] = pos;
+      sh.res[1] = lflags;
+    }
+  }
+  row_sync<W>();
+  return sh.res[0];
 }
 
 // ---------------------------------------------------------------------------
@@ -590,33 +666,13 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   const uint32_t row_bytes = static_cast<uint32_t>(V * esz);
   const unsigned char* grow = static_cast<const unsigned char*>(a.logits) + static_cast<int64_t>(b) * a.row_stride * esz;
 
-  // ---- first loads: offsets and the suppress words of this warp's quads
-  //      (L2-resident: every row reads them) ---------------------------------
-  int o0 = 0, o1 = 0;
-  if (history) {
-    o0 = __ldg(a.offsets + b);
-    o1 = __ldg(a.offsets + b + 1);
-  }
-  uint32_t supw[RPW];
-#pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int h = lane + 32 * (rb0 + i);
-    supw[i] = (suppress && 4 * h < V) ? __ldg(reinterpret_cast<const uint32_t*>(suppress + 4 * h)) : 0u;
-  }
-  {
-    // zero the histograms and the presence flags
-    uint4* hz = reinterpret_cast<uint4*>(&sh.hist[0][0]);
-    for (int i = t; i < 2 * NBINS / 4; i += NT) hz[i] = make_uint4(0, 0, 0, 0);
-    uint4* sz = reinterpret_cast<uint4*>(sh.u.seen);
-    for (int i = t; i < Smem::VMAX / 16; i += NT) sz[i] = make_uint4(0, 0, 0, 0);
-  }
-  row_sync<W>();
-
   // ---- the row's logits stream into shared memory (bulk copies, no
-  //      multicast) while the history is scattered.  bf16: warp w's block of
-  //      the row (bytes [256 RPW w, +256 RPW)) lands in the upper half of its
-  //      own fp32 region ([512 RPW w, +512 RPW)), where that warp alone widens
-  //      it in place; fp32 lands as is ------------------------------------------
+  //      multicast), issued before any other memory access of the issuing
+  //      thread (the mbarrier-init fence would otherwise wait for its loads),
+  //      and land while the history is scattered.  fp32 lands as is; bf16:
+  //      warp w's block of the row (bytes [256 RPW w, +256 RPW)) lands in the
+  //      upper half of its own fp32 region ([512 RPW w, +512 RPW)), where that
+  //      warp alone widens it in place ------------------------------------------
   if (t == 0) {
     mbar_init(&sh.bar, 1);
     fence_mbar_init();
@@ -634,6 +690,35 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
       bulk_g2s(reinterpret_cast<unsigned char*>(sh.row), grow, row_bytes, &sh.bar);
     }
   }
+
+  // ---- first loads: offsets and the suppress words of this warp's quads
+  //      (L2-resident: every row reads them) ---------------------------------
+  int o0 = 0, o1 = 0;
+  if (history) {
+    o0 = __ldg(a.offsets + b);
+    o1 = __ldg(a.offsets + b + 1);
+  }
+  const float T = a.temperature ? __ldg(a.temperature + b) : a.temperature_default;
+  const float pen = a.penalty ? __ldg(a.penalty + b) : a.penalty_default;
+  const float top_p = a.top_p ? __ldg(a.top_p + b) : a.top_p_default;
+  const int kk = a.top_k ? __ldg(a.top_k + b) : a.K;
+  const int min_new = a.min_new ? __ldg(a.min_new + b) : a.min_new_default;
+  const float u = a.uniforms ? __ldg(a.uniforms + b) : 0.0f;
+  const int cur_given = a.cur_len ? __ldg(a.cur_len + b) : -1;
+  uint32_t supw[RPW];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int h = lane + 32 * (rb0 + i);
+    supw[i] = (suppress && 4 * h < V) ? __ldg(reinterpret_cast<const uint32_t*>(suppress + 4 * h)) : 0u;
+  }
+  {
+    // zero the histograms and the presence flags
+    uint4* hz = reinterpret_cast<uint4*>(&sh.hist[0][0]);
+    for (int i = t; i < 2 * NBINS / 4; i += NT) hz[i] = make_uint4(0, 0, 0, 0);
+    uint4* sz = reinterpret_cast<uint4*>(sh.u.seen);
+    for (int i = t; i < Smem::VMAX / 16; i += NT) sz[i] = make_uint4(0, 0, 0, 0);
+  }
+  row_sync<W>();
 
   // presence scatter from the packed history (RepetitionPenalty's gather
   // set); racing stores of the same byte need no atomics
@@ -682,13 +767,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
       }
     }
   }
-  const float T = a.temperature ? __ldg(a.temperature + b) : a.temperature_default;
-  const float pen = a.penalty ? __ldg(a.penalty + b) : a.penalty_default;
-  const float top_p = a.top_p ? __ldg(a.top_p + b) : a.top_p_default;
-  const int kk = a.top_k ? __ldg(a.top_k + b) : a.K;
-  const int min_new = a.min_new ? __ldg(a.min_new + b) : a.min_new_default;
-  const float u = a.uniforms ? __ldg(a.uniforms + b) : 0.0f;
-  const int cur = a.cur_len ? __ldg(a.cur_len + b) : hist_len;
+  const int cur = a.cur_len ? cur_given : hist_len;
   const bool gate = eos_id >= 0 && eos_id < V && cur < min_new;
 
   int id = 0, flags = 0;
@@ -724,18 +803,27 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     return;
   }
 
-  // the exact s of entry v: the processors of the first pass and s = x'/T,
-  // recomputed from the logits in global memory
-  auto exact_s = [&](int v) -> float {
+  // the exact x' of entry v (suppress, EOS gate, repetition penalty) and
+  // s = x'/T, recomputed from the logits in global memory (L2-resident)
+  auto exact_x = [&](int v) -> float {
     float x = BF16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(grow)[v])
                    : reinterpret_cast<const float*>(grow)[v];
     if (suppress && suppress[v]) x = NEG_SUPPRESS;
     if (gate && v == eos_id) x = -INFINITY;
     if ((sh.appb[v >> 2] >> (v & 3)) & 1u) x = x > 0.0f ? __fdiv_rn(x, pen) : __fmul_rn(x, pen);
+    return x;
+  };
+  auto exact_s = [&](int v) -> float {
+    const float x = exact_x(v);
     return divT ? __fdiv_rn(x, T) : x;
   };
   float lm = -INFINITY, gv = -INFINITY;  // running max of s; torch.argmax of s (greedy rows)
   int gi = 0x7fffffff;
+  // candidate rows: the largest approximate value (x * RN(1/pen) for the
+  // entries still to divide) and whether any is NaN, seen in the first pass
+  const float rpen = __frcp_rn(pen);
+  float amax = -INFINITY;
+  bool anan = false;
 
   // ---- first pass: suppress (-1e9, talker_unified_modules.py:409), the EOS
   //      gate (-inf), the repetition penalty.  Candidate rows defer the
@@ -743,21 +831,24 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   //      whole-vocabulary rows compute s = x'/T here.  Branch-free per entry:
   //      the selects replace data-dependent branches ------------------------
   {
-    // this warp's staged bf16 block: local round i at byte 256 i + 8 l
-    const uint2* stg = reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned char*>(sh.row) +
-                                                      512 * RPW * wi + 256 * RPW);
+    // this warp's staged bf16 block (local round i at byte 256 i + 8 l of the
+    // upper half of its region) is read whole before the widened quads
+    // overwrite the region
+    uint2 stq[BF16 ? RPW : 1];
+    if (BF16) {
+      const uint2* stg = reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned char*>(sh.row) +
+                                                        512 * RPW * wi + 256 * RPW);
+#pragma unroll
+      for (int i = 0; i < RPW; ++i) stq[i] = (4 * (lane + 32 * (rb0 + i)) < V) ? stg[lane + 32 * i] : make_uint2(0u, 0u);
+      __syncwarp();
+    }
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
       const int h = lane + 32 * (rb0 + i);
       const bool in = 4 * h < V;
       float v[4];
       if (BF16) {
-        // widening in order within this warp's region: round i reads bf16
-        // bytes [256 RPW + 256 i, +256) and writes fp32 bytes [512 i, +512)
-        // of the region, so the writes end where round i+1's reads begin, at
-        // the latest (i <= RPW - 1)
-        const uint2 q = in ? stg[lane + 32 * i] : make_uint2(0u, 0u);
-        __syncwarp();
+        const uint2 q = stq[BF16 ? i : 0];
         v[0] = bf16_bits_to_f32(q.x & 0xffffu);
         v[1] = bf16_bits_to_f32(q.x >> 16);
         v[2] = bf16_bits_to_f32(q.y & 0xffffu);
@@ -779,7 +870,11 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
           float x = ((supw[i] >> (8 * j)) & 0xffu) ? NEG_SUPPRESS : v[j];
           x = (gate && 4 * h + j == eos_id) ? -INFINITY : x;
           if (cand_path) {
-            x = (ap && !(x > 0.0f)) ? __fmul_rn(x, pen) : x;
+            // the approximate value: x * pen for present entries <= 0 (exact),
+            // x * RN(1/pen) for present entries > 0 (within 2 ulps of x / pen)
+            x = ap ? __fmul_rn(x, x > 0.0f ? rpen : pen) : x;
+            amax = fmaxf(amax, x);
+            anan |= x != x;
           } else {
             const float dv = __fdiv_rn(x, pen), mv = __fmul_rn(x, pen);
             x = ap ? (x > 0.0f ? dv : mv) : x;
@@ -795,44 +890,120 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         sh.row[h] = make_float4(v[0], v[1], v[2], v[3]);
         sh.appb[h] = static_cast<uint8_t>(app);
       }
-      if (BF16) __syncwarp();
     }
   }
   row_sync<W>();  // the row is processed; the presence flags are dead
 
   bool done = false;
   if (cand_path) {
-    // ---- few survivors: select on approximate keys (x * RN(1/pen) instead
-    //      of x / pen, within a few ulps), resolve exactly on the candidates
-    //      within 40 key units of the threshold or above ----------------------
-    const float rpen = __frcp_rn(pen);
-    auto akeys = [&](int r, uint32_t (&key)[4]) -> uint32_t {
-      const int h = lane + 32 * r;
-      if (4 * h >= V) {
+    // ---- few survivors: the row holds approximate values (x * RN(1/pen)
+    //      instead of x / pen for present entries > 0, within 2 ulps); select
+    //      a threshold on them, resolve exactly on the candidates ------------
+    //
+    // Two histograms of d = max - value: bins 1 wide over d < 255, then bins
+    // 1/64 wide over the two unit bins from the one holding the K-th largest.
+    // With every value in [-2000, 2000] an ulp is <= 2^-12, so the
+    // approximation error plus any temperature-tie window (a few ulps) stays
+    // far inside one fine bin: every entry above the fine bin holding the
+    // K-th largest, in it, or in the next one down is a candidate.  Otherwise
+    // (wider values, NaN, the K-th below d = 253) a radix select on the
+    // approximate keys with a 40-unit margin.
+    amax = X.max_f(anan ? INFINITY : amax);
+    auto dist = [&](float v) -> float { return __fsub_rn(amax, v); };
+    bool linear = fabsf(amax) <= 2000.0f;
+    uint32_t ba = 0, bb = 0;  // unit bin and fine bin of the K-th largest
+    if (linear) {
+#pragma unroll 2
+      for (int r = rb0; r < rb1; ++r) {
+        const int h = lane + 32 * r;
+        if (4 * h >= V) continue;
+        const float4 q = sh.row[h];
+        const float v[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) key[j] = 0u;
-        return 0u;
+        for (int j = 0; j < 4; ++j) {
+          const float d = dist(v[j]);
+          if (d < 255.0f) atomicAdd(&sh.hist[0][255u - static_cast<uint32_t>(d)], 1u);
+        }
       }
-      const float4 q = sh.row[h];
-      const float v[4] = {q.x, q.y, q.z, q.w};
-      const uint32_t app = sh.appb[h];
+      row_sync<W>();
+      if (wi == 0) {
+        uint32_t d, c, knew;
+        warp_scan_count_desc(sh.hist[0], static_cast<uint32_t>(K), d, c, knew);
+        if (lane == 0) {
+          sh.sel[0] = d;
+          sh.sel[1] = knew;
+        }
+      }
+      row_sync<W>();
+      ba = 255u - sh.sel[0];
+      const uint32_t krem = sh.sel[1];
+      linear = ba <= 253u;
+      if (linear) {
+        const float d0 = static_cast<float>(ba);
+#pragma unroll 2
+        for (int r = rb0; r < rb1; ++r) {
+          const int h = lane + 32 * r;
+          if (4 * h >= V) continue;
+          const float4 q = sh.row[h];
+          const float v[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) key[j] = f2key((((app >> j) & 1u) && v[j] > 0.0f) ? __fmul_rn(v[j], rpen) : v[j]);
-      return 15u;
-    };
-    const uint32_t thr = row_select<R, W>(sh, wi, K, WCAP / 2 + K / 2, akeys);
-    const uint32_t lo = thr > 40u ? thr - 40u : 0u;
+          for (int j = 0; j < 4; ++j) {
+            const float e = __fmul_rn(__fsub_rn(dist(v[j]), d0), 64.0f);
+            if (e >= 0.0f && e < 128.0f) atomicAdd(&sh.hist[0][255u - static_cast<uint32_t>(e)], 1u);
+          }
+        }
+        row_sync<W>();
+        if (wi == 0) {
+          uint32_t d, c, knew;
+          warp_scan_count_desc(sh.hist[0], krem, d, c, knew);
+          if (lane == 0) sh.sel[0] = d;
+        }
+        row_sync<W>();
+        bb = 255u - sh.sel[0];
+      }
+    }
+    uint32_t lo = 0;
+    if (!linear) {
+      const uint32_t thr = row_select<R, W>(sh, wi, K, WCAP / 2 + K / 2, [&](int r, uint32_t (&key)[4]) -> uint32_t {
+        const int h = lane + 32 * r;
+        if (4 * h >= V) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) key[j] = 0u;
+          return 0u;
+        }
+        const float4 q = sh.row[h];
+        key[0] = f2key(q.x);
+        key[1] = f2key(q.y);
+        key[2] = f2key(q.z);
+        key[3] = f2key(q.w);
+        return 15u;
+      });
+      lo = thr > 40u ? thr - 40u : 0u;
+    }
     // candidates: masks per quad, then records in vocabulary order
+    const float dcut = static_cast<float>(ba);
+    const float ecut = static_cast<float>(bb + 2u);  // fine bins <= bb + 1
     uint32_t cnt = 0;
 #pragma unroll 2
     for (int r = rb0; r < rb1; ++r) {
-      uint32_t key[4];
-      const uint32_t act = akeys(r, key);
+      const int h = lane + 32 * r;
       uint32_t cm = 0;
+      if (4 * h < V) {
+        const float4 q = sh.row[h];
+        const float v[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (((act >> j) & 1u) && key[j] >= lo) cm |= 1u << j;
-      sh.cmask[lane + 32 * r] = static_cast<uint8_t>(cm);
+        for (int j = 0; j < 4; ++j) {
+          bool c;
+          if (linear) {
+            const float d = dist(v[j]);
+            c = d < dcut || __fmul_rn(__fsub_rn(d, dcut), 64.0f) < ecut;
+          } else {
+            c = f2key(v[j]) >= lo;
+          }
+          cm |= (c ? 1u : 0u) << j;
+        }
+      }
+      sh.cmask[h] = static_cast<uint8_t>(cm);
       cnt += __popc(cm);
     }
 #pragma unroll
@@ -842,39 +1013,33 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     const int n = static_cast<int>(n32);
     const int n4 = (n + 3) & ~3;
     if (n <= WCAP) {
-      // records {0, index, x' (not yet divided by pen), 1 if x / pen is due}
+      // records {0, index, 0, 0}; the list's first step fills in x' and s
 #pragma unroll 2
       for (int r = rb0; r < rb1; ++r) {
         const int h = lane + 32 * r;
         const uint32_t cm = sh.cmask[h];
         uint32_t tot;
-        uint32_t p = base + warp_excl_scan_u(__popc(cm), tot);
-        if (cm) {
-          const float4 f = sh.row[h];
-          const float v[4] = {f.x, f.y, f.z, f.w};
-          const uint32_t app = sh.appb[h];
+        uint32_t p = base + warp_excl_small(__popc(cm), tot);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if ((cm >> j) & 1u) {
-              sh.u.cand[p] = make_uint4(0u, static_cast<uint32_t>(4 * h + j), __float_as_uint(v[j]),
-                                        (((app >> j) & 1u) && v[j] > 0.0f) ? 1u : 0u);
-              ++p;
-            }
-        }
+        for (int j = 0; j < 4; ++j)
+          if ((cm >> j) & 1u) {
+            sh.u.cand[p] = make_uint4(0u, static_cast<uint32_t>(4 * h + j), 0u, 0u);
+            ++p;
+          }
         base += tot;
       }
     }
     row_sync<W>();
     if (n <= WCAP) {
-      // ---- the list, all threads: exact x' and s per candidate (padding
-      //      records never outrank and weigh nothing) --------------------------
+      // ---- the list, all threads: exact x' (recomputed from the logits in
+      //      L2, one load round trip for all candidates at once) and s per
+      //      candidate; padding records never outrank and weigh nothing -------
       for (int p = t; p < n4; p += NT) {
         if (p < n) {
-          const uint4 c = sh.u.cand[p];
-          float x = __uint_as_float(c.z);
-          if (c.w) x = __fdiv_rn(x, pen);
+          const uint32_t v = sh.u.cand[p].y;
+          const float x = exact_x(static_cast<int>(v));
           const float s = greedy ? x : __fdiv_rn(x, T);
-          sh.u.cand[p] = make_uint4(__float_as_uint(s), c.y, __float_as_uint(x), 0u);
+          sh.u.cand[p] = make_uint4(__float_as_uint(s), v, __float_as_uint(x), 0u);
         } else {
           sh.u.cand[p] = make_uint4(0xff800000u, 0x7fffffffu, 0xff800000u, 0u);
         }
@@ -897,71 +1062,72 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         flags = Q3S_ROW_GREEDY;
         done = true;
       } else {
-        // HF TopK keeps s >= the K-th largest s (ties kept): all-pairs ranks;
-        // every rank loop also sees the list's maximum
-        float sk_loc = INFINITY, m_loc = -INFINITY;
-        for (int p = t; p < n; p += NT) {
-          const float sp = __uint_as_float(sh.u.cand[p].x);
+        // Every thread walks the whole list, so the list's maximum and the
+        // proof window (below) are known to all threads without an exchange;
+        // each thread ranks its own positions: HF TopK keeps s >= the K-th
+        // largest s (ties kept), i.e. fewer than K entries above.
+        unsigned long long* mq = reinterpret_cast<unsigned long long*>(sh.hist);  // masses (the histograms are done)
+        if (t == 0) sh.res[3] = 0;
+        float m = -INFINITY;
+        bool inwin = true;
+        for (int p = t; p < (n > NT ? n : NT); p += NT) {
+          const float sp = p < n ? __uint_as_float(sh.u.cand[p].x) : INFINITY;
           int above = 0;
-          float m = -INFINITY;
+          m = -INFINITY;
+          inwin = true;
           for (int q = 0; q < n4; q += 4) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const float so = __uint_as_float(sh.u.cand[q + v].x);
               above += so > sp;
               m = fmaxf(m, so);
+              const float ao = fabsf(so);
+              inwin &= (q + v >= n) || (ao >= 0x1p-100f && ao <= 0x1p100f);
             }
           }
-          const bool sv = above < K;
-          sh.keep[p] = sv;
-          sh.u.cand[p].w = __float_as_uint(sv ? softmax_weight(sp, m) : 0.0f);
-          if (sv) sk_loc = fminf(sk_loc, sp);
-          m_loc = m;
+          if (p < n4) {
+            const bool sv = p < n && above < K;
+            const float wgt = sv ? softmax_weight(sp, m) : 0.0f;
+            sh.keep[p] = sv;
+            sh.u.cand[p].w = __float_as_uint(wgt);
+            mq[p] = sv ? mass_fixed(wgt) : 0ull;
+          }
         }
-        for (int p = n + t; p < n4; p += NT) sh.keep[p] = 0;
-        const float sk = fabsf(X.min_f(sk_loc));
-        const float mm = X.max_f(m_loc);
         row_sync<W>();
-        // quotients far from 1 may merge more than 40 key units of x': the
-        // candidate set is proven complete only inside this window
-        if (mm != -INFINITY && sk >= 0x1p-100f && sk <= 0x1p100f) {
+        // quotients far from 1 may merge more than 40 key units of x' (or
+        // more than one linear bin): the candidate set is proven complete
+        // only while every candidate's |s| stays inside this window
+        if (m != -INFINITY && inwin) {
           uint8_t* kout = sh.cmask;  // kept entries
           if (top_p < 1.0f) {
-            unsigned long long lq = 0;
-            for (int p = t; p < n; p += NT)
-              if (sh.keep[p]) lq += mass_fixed(__uint_as_float(sh.u.cand[p].w));
-            const unsigned long long Zq = X.sum_q(lq);
+            // total survivor mass, the same in every thread (fixed order)
+            unsigned long long Zq = 0;
+            for (int q = 0; q < n4; ++q) Zq += mq[q];
             const float frac = __fsub_rn(1.0f, top_p);
             const unsigned long long tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
             if (tau >= Zq) {
               // only the ascending-last survivor stays: largest s, then index
-              unsigned long long best = 0;
-              for (int p = t; p < n; p += NT)
-                if (sh.keep[p]) {
-                  const unsigned long long key = (static_cast<unsigned long long>(f2key(__uint_as_float(
-                                                      sh.u.cand[p].x))) << 32) | sh.u.cand[p].y;
-                  best = key > best ? key : best;
+              for (int p = t; p < n; p += NT) {
+                bool last = sh.keep[p];
+                if (last) {
+                  const float sp = __uint_as_float(sh.u.cand[p].x);
+                  for (int q = 0; q < n; ++q) {
+                    const float so = __uint_as_float(sh.u.cand[q].x);
+                    last &= !(sh.keep[q] && (so > sp || (so == sp && sh.u.cand[q].y > sh.u.cand[p].y)));
+                  }
                 }
-              best = X.max_q(best);
-              for (int p = t; p < n; p += NT)
-                kout[p] = sh.keep[p] && sh.u.cand[p].y == static_cast<uint32_t>(best & 0xffffffffu);
+                kout[p] = last;
+              }
             } else {
-              flags |= row_cut_list<R, W>(sh.u.cand, sh.keep, kout, n, n4, tau, 0ull, Zq / 1000000ull, X);
+              row_cut_list<W>(sh.u.cand, sh.keep, mq, kout, n, n4, tau, 0ull, Zq / 1000000ull, &sh.res[3]);
             }
           } else {
             for (int p = t; p < n; p += NT) kout[p] = sh.keep[p];
           }
           row_sync<W>();
-          if (wi == 0) {
-            int lflags = 0;
-            const int pos = warp_draw_list(sh.u.cand, kout, n, u, lflags);
-            if (lane == 0) {
-              sh.res[0] = static_cast<int>(sh.u.cand[pos].y);
-              sh.res[1] = lflags;
-            }
-          }
-          row_sync<W>();
-          id = sh.res[0];
+          flags |= sh.res[3];
+          const int pos = row_draw_list<R, W>(sh, kout, reinterpret_cast<float*>(sh.hist), n, u);
+          id = static_cast<int>(sh.u.cand[pos].y);
           flags |= sh.res[1];
           done = true;
         }
@@ -969,20 +1135,16 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     }
     if (!done) {
       // the candidate set overflowed or left the proven window: exact s for
-      // the whole row in place
-#pragma unroll 2
+      // the whole row, recomputed from the logits (the row holds approximate
+      // values)
+#pragma unroll 1
       for (int r = rb0; r < rb1; ++r) {
         const int h = lane + 32 * r;
         if (4 * h >= V) continue;
-        const float4 f = sh.row[h];
-        float v[4] = {f.x, f.y, f.z, f.w};
-        const uint32_t app = sh.appb[h];
+        float v[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float x = v[j];
-          const float dv = __fdiv_rn(x, pen);
-          x = (((app >> j) & 1u) && x > 0.0f) ? dv : x;
-          if (divT) x = __fdiv_rn(x, T);
+          const float x = exact_s(4 * h + j);
           lm = fmaxf(lm, x);
           if (greedy && arg_better(x, 4 * h + j, gv, gi)) {
             gv = x;
@@ -1133,7 +1295,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
                 const int h = lane + 32 * r;
                 const uint32_t cm = sh.cmask[h];
                 uint32_t tot;
-                uint32_t p = base + warp_excl_scan_u(__popc(cm), tot);
+                uint32_t p = base + warp_excl_small(__popc(cm), tot);
                 if (cm) {
                   const float4 f = sh.row[h];
                   const float wv[4] = {f.x, f.y, f.z, f.w};
@@ -1151,19 +1313,25 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
               // exact s of the crossing bin's entries, the exact cut over
               // them, and the removed entries' weights zeroed in the row
               const int n4 = (n + 3) & ~3;
+              unsigned long long* mq = reinterpret_cast<unsigned long long*>(sh.hist);  // (the histogram is done)
+              if (t == 0) sh.res[3] = 0;
               for (int p = t; p < n4; p += NT) {
-                if (p < n)
+                if (p < n) {
                   sh.u.cand[p].x = __float_as_uint(exact_s(static_cast<int>(sh.u.cand[p].y)));
-                else
+                  mq[p] = mass_fixed(__uint_as_float(sh.u.cand[p].w));
+                } else {
                   sh.u.cand[p] = make_uint4(0xff800000u, 0x7fffffffu, 0u, 0u);
+                  mq[p] = 0ull;
+                }
                 sh.keep[p] = p < n;
               }
               row_sync<W>();
               uint8_t* kout = sh.cmask;
-              flags |= row_cut_list<R, W>(sh.u.cand, sh.keep, kout, n, n4, tau, below, eps, X);
+              row_cut_list<W>(sh.u.cand, sh.keep, mq, kout, n, n4, tau, below, eps, &sh.res[3]);
               for (int p = t; p < n; p += NT)
                 if (!kout[p]) rowf[sh.u.cand[p].y] = 0.0f;
               row_sync<W>();
+              flags |= sh.res[3];
             } else {
               // the crossing bin holds too many entries: an exact radix cut
               // over the survivors of that bin and above, keys from the exact

@@ -23,7 +23,7 @@ DRAW_GUMBEL, DRAW_ICDF = 0, 1
 DTYPE_F32, DTYPE_BF16 = 0, 1
 CP_DIRECT, CP_ROTATE = 0, 1
 POLICY_AUTO, POLICY_CTA, POLICY_WARP = 0, 1, 2
-POLICY_ROW_W = {1: 3, 2: 4, 4: 5, 8: 6}
+POLICY_ROW_W = {1: 3, 2: 4, 4: 5, 8: 6, "max": 7}
 
 ROW_DRAW_BOUNDARY, ROW_TOPP_BOUNDARY, ROW_GREEDY, ROW_FALLBACK = 1, 2, 4, 8
 DEVERR_HISTORY_ID, DEVERR_OFFSETS, DEVERR_NO_MASS, DEVERR_WAIT_TIMEOUT, DEVERR_CANDIDATES = 1, 2, 4, 8, 16
