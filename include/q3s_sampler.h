@@ -190,7 +190,7 @@ uint32_t q3s_desc_size(int32_t which);
  * a tuning and test knob with no counterpart in the reference interface):
  * the register-resident CTA-per-row kernel, or the shared-memory-resident
  * row kernel with W warps per row (W chosen from the batch size, or forced).
- * AUTO picks the shared-memory kernel for large batches.  All return the
+ * AUTO picks the shared-memory kernel wherever it applies.  All return the
  * same ids, except that a draw or a top-p cut within 1e-6 of a
  * cumulative-mass edge (flagged in row_flags) may land on either side.
  * Steps that need token_counts, col_shift, processed_logits or counts_out,

@@ -70,7 +70,7 @@ struct CpArgs {
 // V % 8 == 0; `warps` (1, 2, 4 or 8; anything else: the widest variant,
 // 12 warps for V > 2048 and 16 below) warps per row.
 cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st, int warps);
-// Warps per row for a batch size on `sm_count` SMs.
+// Warps per row for a batch size on `sm_count` SMs (0: the widest variant).
 int smem_warps_for(int batch, int sm_count);
 
 }  // namespace q3s

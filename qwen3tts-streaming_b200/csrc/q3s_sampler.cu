@@ -1088,8 +1088,6 @@ q3s_status launch_rows(const q3s::SampleArgs& a, bool bf16, cudaStream_t st) {
 
 // Process-wide kernel policy (q3s_set_kernel_policy).
 int g_policy = Q3S_POLICY_AUTO;
-// Batch size from which AUTO takes warp-per-row.
-constexpr int WARP_MIN_ROWS = 256;
 
 int device_sm_count() {
   static int cache[64] = {0};
@@ -1251,7 +1249,7 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
                        !a.counts_out && V % 8 == 0 && V > 1024 && V <= 3072 && a.vec_logits &&
                        (!a.suppress || a.vec_suppress);
   const int policy = __atomic_load_n(&g_policy, __ATOMIC_RELAXED);
-  if (warp_ok && policy != Q3S_POLICY_CTA && (policy != Q3S_POLICY_AUTO || a.B >= WARP_MIN_ROWS)) {
+  if (warp_ok && policy != Q3S_POLICY_CTA) {
     int warps = q3s::smem_warps_for(a.B, device_sm_count());
     if (policy == Q3S_POLICY_ROW_W1) warps = 1;
     if (policy == Q3S_POLICY_ROW_W2) warps = 2;

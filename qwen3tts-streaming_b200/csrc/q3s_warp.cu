@@ -45,10 +45,12 @@ cudaError_t launch_r(const SampleArgs& a, bool bf16, cudaStream_t st, int w) {
 }  // namespace
 
 int smem_warps_for(int batch, int sm_count) {
-  // measured on B200 (V=3072, configs 1/3/4): a row's passes are chains of
-  // dependent shared-memory work, so spreading it over 4 warps beats running
-  // more rows side by side up to B=4096; small batches take 8
-  return batch >= 2 * sm_count ? 4 : 8;
+  // measured on B200 (V=3072, configs 1/3/4): up to one row per SM a row is
+  // latency-bound and takes the widest variant; up to two, 8 warps; beyond,
+  // 4 warps per row (more rows side by side)
+  if (batch <= sm_count) return 0;  // widest
+  if (batch <= 2 * sm_count) return 8;
+  return 4;
 }
 
 cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st, int warps) {

@@ -76,6 +76,41 @@ Q3S_DEV void warp_scan_count_desc(uint32_t* hist, uint32_t krem, uint32_t& d, ui
   __syncwarp();
 }
 
+// As warp_scan_count_desc, without clearing the bins (several warps may scan
+// the same histogram).
+Q3S_DEV void warp_scan_count_desc_keep(const uint32_t* hist, uint32_t krem, uint32_t& d, uint32_t& knew) {
+  const int lane = lane_id();
+  const uint4* hb = reinterpret_cast<const uint4*>(hist) + 2 * lane;
+  const uint4 a = hb[0], b = hb[1];
+  const uint32_t c[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  const uint32_t s = (c[0] + c[1]) + (c[2] + c[3]) + (c[4] + c[5]) + (c[6] + c[7]);
+  uint32_t suf = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t n = __shfl_down_sync(FULL, suf, o);
+    if (lane + o < 32) suf += n;
+  }
+  const uint32_t above = suf - s;
+  const bool hit = above < krem && krem <= suf;
+  uint32_t md = 0, mk = 0;
+  if (hit) {
+    uint32_t acc = above;
+    bool found = false;
+#pragma unroll
+    for (int i = 7; i >= 0; --i) {
+      if (!found && acc + c[i] >= krem) {
+        found = true;
+        md = static_cast<uint32_t>(8 * lane + i);
+        mk = krem - acc;
+      }
+      acc += c[i];
+    }
+  }
+  const int src = (__ffs(__ballot_sync(FULL, hit)) - 1) & 31;
+  d = __shfl_sync(FULL, md, src);
+  knew = __shfl_sync(FULL, mk, src);
+}
+
 // Exact fixed-point masses (hi/lo histograms), bins ascending: the first bin
 // where below + mass up to it exceeds tau, and the mass before it.
 Q3S_DEV void warp_scan_mass_asc(uint32_t* hhi, uint32_t* hlo, unsigned long long below, unsigned long long tau,
@@ -211,6 +246,14 @@ Q3S_DEV int warp_draw_list(const float* wk, int n, float u, int& flags) {
   return src * P + rsel;
 }
 
+// Lanes per candidate for a list of n4 entries and NT threads: the largest
+// power of two <= NT / n4, at most 8 (at least 1).
+Q3S_DEV int list_lanes(int n4, int nt) {
+  int tp = 1;
+  while (tp < 8 && 2 * tp * max(n4, 1) <= nt) tp *= 2;
+  return tp;
+}
+
 // Exclusive prefix over the lanes of a small count (0..7) and the warp total,
 // from three ballots.
 Q3S_DEV uint32_t warp_excl_small(uint32_t c, uint32_t& total) {
@@ -313,6 +356,7 @@ struct alignas(16) RowSmem {
   uint32_t sel[4];                       // a leader warp's results
   unsigned long long selq[4];
   int res[4];
+  int lcnt[2];                           // list counters (band, crossing-bin entries)
   uint64_t bar;                          // completion of the logits bulk copy
 };
 
@@ -666,31 +710,6 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   const uint32_t row_bytes = static_cast<uint32_t>(V * esz);
   const unsigned char* grow = static_cast<const unsigned char*>(a.logits) + static_cast<int64_t>(b) * a.row_stride * esz;
 
-  // ---- the row's logits stream into shared memory (bulk copies, no
-  //      multicast), issued before any other memory access of the issuing
-  //      thread (the mbarrier-init fence would otherwise wait for its loads),
-  //      and land while the history is scattered.  fp32 lands as is; bf16:
-  //      warp w's block of the row (bytes [256 RPW w, +256 RPW)) lands in the
-  //      upper half of its own fp32 region ([512 RPW w, +512 RPW)), where that
-  //      warp alone widens it in place ------------------------------------------
-  if (t == 0) {
-    mbar_init(&sh.bar, 1);
-    fence_mbar_init();
-    mbar_expect_tx(&sh.bar, row_bytes);
-    if (BF16) {
-#pragma unroll 1
-      for (int w = 0; w < W; ++w) {
-        const int off = 256 * RPW * w;
-        const int len = min(256 * RPW, static_cast<int>(row_bytes) - off);
-        if (len > 0)
-          bulk_g2s(reinterpret_cast<unsigned char*>(sh.row) + 512 * RPW * w + 256 * RPW, grow + off,
-                   static_cast<uint32_t>(len), &sh.bar);
-      }
-    } else {
-      bulk_g2s(reinterpret_cast<unsigned char*>(sh.row), grow, row_bytes, &sh.bar);
-    }
-  }
-
   // ---- first loads: offsets and the suppress words of this warp's quads
   //      (L2-resident: every row reads them) ---------------------------------
   int o0 = 0, o1 = 0;
@@ -720,6 +739,30 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   }
   row_sync<W>();
 
+  // ---- the row's logits stream into shared memory (bulk copies, no
+  //      multicast), issued by thread 0 after the first barrier (so that no
+  //      other thread waits for the issue) while the history is scattered.  fp32 lands as is; bf16:
+  //      warp w's block of the row (bytes [256 RPW w, +256 RPW)) lands in the
+  //      upper half of its own fp32 region ([512 RPW w, +512 RPW)), where that
+  //      warp alone widens it in place ------------------------------------------
+  if (t == 0) {
+    mbar_init(&sh.bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&sh.bar, row_bytes);
+    if (BF16) {
+#pragma unroll 1
+      for (int w = 0; w < W; ++w) {
+        const int off = 256 * RPW * w;
+        const int len = min(256 * RPW, static_cast<int>(row_bytes) - off);
+        if (len > 0)
+          bulk_g2s(reinterpret_cast<unsigned char*>(sh.row) + 512 * RPW * w + 256 * RPW, grow + off,
+                   static_cast<uint32_t>(len), &sh.bar);
+      }
+    } else {
+      bulk_g2s(reinterpret_cast<unsigned char*>(sh.row), grow, row_bytes, &sh.bar);
+    }
+  }
+
   // presence scatter from the packed history (RepetitionPenalty's gather
   // set); racing stores of the same byte need no atomics
   int hist_len = 0;
@@ -739,11 +782,13 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     const int nrest = nhead + (o1 - mid1);
     const int nwork = nrest + (mid1 - mid0) / 4;  // scalar ids first, then 16-byte groups
     constexpr int U = 8;
-    for (int r0 = t; r0 < nwork; r0 += U * NT) {
+    constexpr int ST = NT;  // scattering threads
+    const int ts = t;
+    for (int r0 = ts; r0 < nwork; r0 += U * ST) {
       int4 ids[U];
 #pragma unroll
       for (int q = 0; q < U; ++q) {
-        const int rr = r0 + q * NT;
+        const int rr = r0 + q * ST;
         ids[q] = make_int4(-1, -1, -1, -1);
         if (rr < nrest)
           ids[q].x = __ldg(hp + (rr < nhead ? o0 + rr : mid1 + (rr - nhead)));
@@ -752,7 +797,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
       }
 #pragma unroll
       for (int q = 0; q < U; ++q) {
-        const int rr = r0 + q * NT;
+        const int rr = r0 + q * ST;
         if (rr >= nwork) continue;
         const int nid = rr < nrest ? 1 : 4;
         const int idv[4] = {ids[q].x, ids[q].y, ids[q].z, ids[q].w};
@@ -926,17 +971,10 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         }
       }
       row_sync<W>();
-      if (wi == 0) {
-        uint32_t d, c, knew;
-        warp_scan_count_desc(sh.hist[0], static_cast<uint32_t>(K), d, c, knew);
-        if (lane == 0) {
-          sh.sel[0] = d;
-          sh.sel[1] = knew;
-        }
-      }
-      row_sync<W>();
-      ba = 255u - sh.sel[0];
-      const uint32_t krem = sh.sel[1];
+      // every warp scans the histogram itself (no broadcast)
+      uint32_t da, krem;
+      warp_scan_count_desc_keep(sh.hist[0], static_cast<uint32_t>(K), da, krem);
+      ba = 255u - da;
       linear = ba <= 253u;
       if (linear) {
         const float d0 = static_cast<float>(ba);
@@ -949,21 +987,23 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float e = __fmul_rn(__fsub_rn(dist(v[j]), d0), 64.0f);
-            if (e >= 0.0f && e < 128.0f) atomicAdd(&sh.hist[0][255u - static_cast<uint32_t>(e)], 1u);
+            if (e >= 0.0f && e < 128.0f) atomicAdd(&sh.hist[1][255u - static_cast<uint32_t>(e)], 1u);
           }
         }
         row_sync<W>();
-        if (wi == 0) {
-          uint32_t d, c, knew;
-          warp_scan_count_desc(sh.hist[0], krem, d, c, knew);
-          if (lane == 0) sh.sel[0] = d;
-        }
-        row_sync<W>();
-        bb = 255u - sh.sel[0];
+        uint32_t db, kb;
+        warp_scan_count_desc_keep(sh.hist[1], krem, db, kb);
+        bb = 255u - db;
       }
+      // every warp has read both histograms once all pass the compaction's
+      // exchange below; the histograms are cleared after it
     }
     uint32_t lo = 0;
     if (!linear) {
+      // the histograms back to zero for the radix passes
+      row_sync<W>();
+      for (int i = t; i < 2 * NBINS; i += NT) (&sh.hist[0][0])[i] = 0u;
+      row_sync<W>();
       const uint32_t thr = row_select<R, W>(sh, wi, K, WCAP / 2 + K / 2, [&](int r, uint32_t (&key)[4]) -> uint32_t {
         const int h = lane + 32 * r;
         if (4 * h >= V) {
@@ -1012,6 +1052,8 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     uint32_t base = X.prefix_u(cnt, n32);
     const int n = static_cast<int>(n32);
     const int n4 = (n + 3) & ~3;
+    // past the exchange every warp is done with the histograms: zero them
+    for (int i = t; i < 2 * NBINS; i += NT) (&sh.hist[0][0])[i] = 0u;
     if (n <= WCAP) {
       // records {0, index, 0, 0}; the list's first step fills in x' and s
 #pragma unroll 2
@@ -1062,70 +1104,144 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         flags = Q3S_ROW_GREEDY;
         done = true;
       } else {
-        // Every thread walks the whole list, so the list's maximum and the
-        // proof window (below) are known to all threads without an exchange;
-        // each thread ranks its own positions: HF TopK keeps s >= the K-th
-        // largest s (ties kept), i.e. fewer than K entries above.
-        unsigned long long* mq = reinterpret_cast<unsigned long long*>(sh.hist);  // masses (the histograms are done)
-        if (t == 0) sh.res[3] = 0;
-        float m = -INFINITY;
-        bool inwin = true;
-        for (int p = t; p < (n > NT ? n : NT); p += NT) {
-          const float sp = p < n ? __uint_as_float(sh.u.cand[p].x) : INFINITY;
-          int above = 0;
-          m = -INFINITY;
-          inwin = true;
-          for (int q = 0; q < n4; q += 4) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const float so = __uint_as_float(sh.u.cand[q + v].x);
-              above += so > sp;
-              m = fmaxf(m, so);
-              const float ao = fabsf(so);
-              inwin &= (q + v >= n) || (ao >= 0x1p-100f && ao <= 0x1p100f);
-            }
-          }
-          if (p < n4) {
-            const bool sv = p < n && above < K;
-            const float wgt = sv ? softmax_weight(sp, m) : 0.0f;
-            sh.keep[p] = sv;
-            sh.u.cand[p].w = __float_as_uint(wgt);
-            mq[p] = sv ? mass_fixed(wgt) : 0ull;
-          }
+        // The list's maximum and the proof window (below) by one exchange.
+        float m = -INFINITY, bad = 0.0f;
+        for (int p = t; p < n; p += NT) {
+          const float sp = __uint_as_float(sh.u.cand[p].x);
+          m = fmaxf(m, sp);
+          const float ap = fabsf(sp);
+          bad = (ap >= 0x1p-100f && ap <= 0x1p100f) ? bad : 1.0f;
         }
-        row_sync<W>();
+        X.max2_f(m, bad);
         // quotients far from 1 may merge more than 40 key units of x' (or
-        // more than one linear bin): the candidate set is proven complete
-        // only while every candidate's |s| stays inside this window
-        if (m != -INFINITY && inwin) {
-          uint8_t* kout = sh.cmask;  // kept entries
-          if (top_p < 1.0f) {
-            // total survivor mass, the same in every thread (fixed order)
-            unsigned long long Zq = 0;
-            for (int q = 0; q < n4; ++q) Zq += mq[q];
-            const float frac = __fsub_rn(1.0f, top_p);
-            const unsigned long long tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
-            if (tau >= Zq) {
-              // only the ascending-last survivor stays: largest s, then index
-              for (int p = t; p < n; p += NT) {
-                bool last = sh.keep[p];
-                if (last) {
-                  const float sp = __uint_as_float(sh.u.cand[p].x);
-                  for (int q = 0; q < n; ++q) {
-                    const float so = __uint_as_float(sh.u.cand[q].x);
-                    last &= !(sh.keep[q] && (so > sp || (so == sp && sh.u.cand[q].y > sh.u.cand[p].y)));
-                  }
-                }
-                kout[p] = last;
-              }
-            } else {
-              row_cut_list<W>(sh.u.cand, sh.keep, mq, kout, n, n4, tau, 0ull, Zq / 1000000ull, &sh.res[3]);
-            }
-          } else {
-            for (int p = t; p < n; p += NT) kout[p] = sh.keep[p];
+        // more than one fine bin): the candidate set is proven complete only
+        // while every candidate's |s| stays inside this window
+        if (m != -INFINITY && bad == 0.0f) {
+          uint8_t* kout = sh.cmask;        // kept entries (positions < 256)
+          uint8_t* small = sh.cmask + 256; // short index lists (positions)
+          if (t == 0) {
+            sh.res[3] = 0;
+            sh.lcnt[0] = 0;
+            sh.lcnt[1] = 0;
           }
           row_sync<W>();
-          flags |= sh.res[3];
+          // ---- HF TopK keeps s >= the K-th largest s (ties kept) ------------
+          if (linear) {
+            // Candidates two fine bins or more above the K-th largest's bin
+            // beat it in exact s (the bins are far wider than the error
+            // window): they survive.  The rest -- the band of fine bins
+            // bb-1 .. bb+1 -- hold the K-th largest as their (K - above)-th
+            // largest; exact ranks there.
+            const float dband = __fadd_rn(dcut, static_cast<float>(static_cast<int>(bb) - 2) * (1.0f / 64.0f));
+            for (int p = t; p < n; p += NT) {
+              const float d = dist(rowf[sh.u.cand[p].y]);
+              const bool inb = d >= dband;
+              sh.keep[p] = !inb;
+              if (inb) small[atomicAdd(&sh.lcnt[0], 1)] = static_cast<uint8_t>(p);
+            }
+            row_sync<W>();
+            const int nb = sh.lcnt[0];
+            const int kb = K - (n - nb);  // rank of the K-th inside the band
+            for (int i = t; i < nb; i += NT) {
+              const int p = small[i];
+              const float sp = __uint_as_float(sh.u.cand[p].x);
+              int above = 0;
+              for (int k = 0; k < nb; ++k) above += __uint_as_float(sh.u.cand[small[k]].x) > sp;
+              sh.keep[p] = above < kb;
+            }
+          } else {
+            // radix-selected candidates: exact all-pairs ranks
+            for (int p = t; p < n; p += NT) {
+              const float sp = __uint_as_float(sh.u.cand[p].x);
+              int above = 0;
+              for (int q = 0; q < n; ++q) above += __uint_as_float(sh.u.cand[q].x) > sp;
+              sh.keep[p] = above < K;
+            }
+          }
+          row_sync<W>();
+          // softmax weights of the survivors; with top-p, their exact
+          // fixed-point masses into the coarse histogram (by the weight's
+          // exponent and top mantissa bits, monotone in s)
+          const bool cut = top_p < 1.0f;
+          constexpr uint32_t LO = (1u << MASS_LO_BITS) - 1u;
+          for (int p = t; p < n; p += NT) {
+            const bool sv = sh.keep[p];
+            const float wgt = sv ? softmax_weight(__uint_as_float(sh.u.cand[p].x), m) : 0.0f;
+            sh.u.cand[p].w = __float_as_uint(wgt);
+            kout[p] = sv;
+            if (cut && sv) {
+              const unsigned long long q = mass_fixed(wgt);
+              if (q) {
+                const uint32_t bn = coarse_bin(wgt);
+                atomicAdd(&sh.hist[0][bn], static_cast<uint32_t>(q >> MASS_LO_BITS));
+                atomicAdd(&sh.hist[1][bn], static_cast<uint32_t>(q) & LO);
+              }
+            }
+          }
+          row_sync<W>();
+          if (cut) {
+            // ---- HF TopPLogitsWarper: remove an entry when the mass at or
+            //      below it in stable ascending order (s asc, index asc) is
+            //      <= tau = floor((1-p) Zq); the crossing bin's entries are
+            //      resolved exactly, those below it go, those above stay ----
+            const float frac = __fsub_rn(1.0f, top_p);
+            if (wi == 0) {
+              unsigned long long Zq, tau, before;
+              uint32_t bstar;
+              warp_scan_mass_total(sh.hist[0], sh.hist[1], frac, Zq, tau, bstar, before);
+              if (lane == 0) {
+                sh.selq[0] = Zq;
+                sh.selq[1] = tau;
+                sh.selq[2] = before;
+                sh.sel[3] = bstar;
+              }
+            }
+            row_sync<W>();
+            const unsigned long long Zq = sh.selq[0], tau = sh.selq[1], below = sh.selq[2];
+            const uint32_t bstar = sh.sel[3];
+            const unsigned long long eps = Zq / 1000000ull;
+            if (tau >= Zq) {
+              // only the ascending-last survivor stays: largest s, then index
+              unsigned long long best = 0;
+              for (int p = t; p < n; p += NT)
+                if (sh.keep[p]) {
+                  const unsigned long long key =
+                      (static_cast<unsigned long long>(f2key(__uint_as_float(sh.u.cand[p].x))) << 32) | p;
+                  best = key > best ? key : best;
+                }
+              best = X.max_q(best);
+              for (int p = t; p < n; p += NT) kout[p] = sh.keep[p] && p == static_cast<int>(best & 0xffffffffu);
+            } else {
+              for (int p = t; p < n; p += NT) {
+                if (!sh.keep[p]) continue;
+                const float wgt = __uint_as_float(sh.u.cand[p].w);
+                const uint32_t bn = mass_fixed(wgt) ? coarse_bin(wgt) : 0u;
+                if (mass_fixed(wgt) && bn == bstar)
+                  small[atomicAdd(&sh.lcnt[1], 1)] = static_cast<uint8_t>(p);
+                else
+                  kout[p] = mass_fixed(wgt) && bn > bstar;
+              }
+              row_sync<W>();
+              const int nc = sh.lcnt[1];
+              bool near = t == 0 && tau - below < eps;
+              for (int i = t; i < nc; i += NT) {
+                const int p = small[i];
+                const float sp = __uint_as_float(sh.u.cand[p].x);
+                unsigned long long cum = below;
+                for (int k = 0; k < nc; ++k) {
+                  const int q = small[k];
+                  const float so = __uint_as_float(sh.u.cand[q].x);
+                  if (so < sp || (so == sp && q <= p)) cum += mass_fixed(__uint_as_float(sh.u.cand[q].w));
+                }
+                const bool kp = cum > tau;
+                kout[p] = kp;
+                near |= kp ? (cum - tau < eps) : (tau - cum < eps);
+              }
+              if (near) atomicOr(&sh.res[3], Q3S_ROW_TOPP_BOUNDARY);
+            }
+            row_sync<W>();
+            flags |= sh.res[3];
+          }
           const int pos = row_draw_list<R, W>(sh, kout, reinterpret_cast<float*>(sh.hist), n, u);
           id = static_cast<int>(sh.u.cand[pos].y);
           flags |= sh.res[1];
@@ -1136,7 +1252,8 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     if (!done) {
       // the candidate set overflowed or left the proven window: exact s for
       // the whole row, recomputed from the logits (the row holds approximate
-      // values)
+      // values); the histograms, used as the list's scratch, back to zero
+      for (int i = t; i < 2 * NBINS; i += NT) (&sh.hist[0][0])[i] = 0u;
 #pragma unroll 1
       for (int r = rb0; r < rb1; ++r) {
         const int h = lane + 32 * r;
