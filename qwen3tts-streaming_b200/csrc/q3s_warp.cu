@@ -11,7 +11,7 @@ namespace {
 
 template <int R, int W>
 cudaError_t launch_smem(const SampleArgs& a, bool bf16, cudaStream_t st) {
-  constexpr size_t dyn = row_smem_bytes<R, W>();
+  const size_t dyn = row_smem_bytes<R, W>(bf16);
   auto kern = bf16 ? sample_smem_kernel<R, W, true> : sample_smem_kernel<R, W, false>;
   // the largest shared-memory carveout, so that ~11 rows fit per SM; set once
   // per (kernel, device)

@@ -324,6 +324,52 @@ Q3S_DEV uint32_t top_bin(float d, float d0, float scale) {
   return e < 255.0f ? static_cast<uint32_t>(e) : 255u;
 }
 
+// As warp_scan_mass_total, without clearing the bins (several warps may scan
+// the same histogram).
+Q3S_DEV void warp_scan_mass_total_keep(const uint32_t* hhi, const uint32_t* hlo, float frac, unsigned long long& Zq,
+                                       unsigned long long& tau, uint32_t& d, unsigned long long& before) {
+  const int lane = lane_id();
+  const uint4* ph = reinterpret_cast<const uint4*>(hhi) + 2 * lane;
+  const uint4* pl = reinterpret_cast<const uint4*>(hlo) + 2 * lane;
+  const uint4 h0 = ph[0], h1 = ph[1], l0 = pl[0], l1 = pl[1];
+  const uint32_t hi[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const uint32_t lo[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  unsigned long long c[8], s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[i] = (static_cast<unsigned long long>(hi[i]) << MASS_LO_BITS) + lo[i];
+    s += c[i];
+  }
+  unsigned long long inc = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long n = __shfl_up_sync(FULL, inc, o);
+    if (lane >= o) inc += n;
+  }
+  Zq = __shfl_sync(FULL, inc, 31);
+  tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
+  const unsigned long long lo0 = inc - s;
+  const bool hit = lo0 <= tau && tau < inc;
+  uint32_t md = 0;
+  unsigned long long mb = 0;
+  if (hit) {
+    unsigned long long acc = lo0;
+    bool found = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (!found && acc + c[i] > tau) {
+        found = true;
+        md = static_cast<uint32_t>(8 * lane + i);
+        mb = acc;
+      }
+      acc += c[i];
+    }
+  }
+  const unsigned bal = __ballot_sync(FULL, hit);
+  d = bal ? __shfl_sync(FULL, md, __ffs(bal) - 1) : 255u;
+  before = bal ? __shfl_sync(FULL, mb, __ffs(bal) - 1) : Zq;
+}
+
 Q3S_DEV uint32_t coarse_bin(float w) {
   const int e = static_cast<int>(__float_as_uint(w) >> COARSE_SHIFT) - COARSE_BIN0;
   return static_cast<uint32_t>(min(255, max(0, e)));
@@ -680,9 +726,10 @@ Q3S_DEV int row_draw_list(RowSmem<R, W>& sh, const uint8_t* kout, float* wk, int
 // the kernel
 // ---------------------------------------------------------------------------
 
+// Dynamic shared memory per row: RowSmem, then (bf16 rows) the row as loaded.
 template <int R, int W>
-constexpr size_t row_smem_bytes() {
-  return sizeof(RowSmem<R, W>);
+constexpr size_t row_smem_bytes(bool bf16) {
+  return sizeof(RowSmem<R, W>) + (bf16 ? 2 * RowSmem<R, W>::VMAX : 0);
 }
 
 template <int R, int W, bool BF16>
@@ -692,6 +739,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   constexpr int RPW = Smem::RPW;
   constexpr int NT = 32 * W;
   Smem& sh = *reinterpret_cast<Smem*>(q3s_row_smem);
+  uint16_t* const stage = reinterpret_cast<uint16_t*>(q3s_row_smem + sizeof(Smem));  // bf16 row as loaded
   const int t = static_cast<int>(threadIdx.x);
   const int wi = t >> 5;
   const int lane = t & 31;
@@ -741,26 +789,14 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
 
   // ---- the row's logits stream into shared memory (bulk copies, no
   //      multicast), issued by thread 0 after the first barrier (so that no
-  //      other thread waits for the issue) while the history is scattered.  fp32 lands as is; bf16:
-  //      warp w's block of the row (bytes [256 RPW w, +256 RPW)) lands in the
-  //      upper half of its own fp32 region ([512 RPW w, +512 RPW)), where that
-  //      warp alone widens it in place ------------------------------------------
+  //      other thread waits for the issue) while the history is scattered:
+  //      fp32 rows into the row buffer, bf16 rows into their staging buffer
+  //      (kept: the exact values of candidates are read back from it) -------
   if (t == 0) {
     mbar_init(&sh.bar, 1);
     fence_mbar_init();
     mbar_expect_tx(&sh.bar, row_bytes);
-    if (BF16) {
-#pragma unroll 1
-      for (int w = 0; w < W; ++w) {
-        const int off = 256 * RPW * w;
-        const int len = min(256 * RPW, static_cast<int>(row_bytes) - off);
-        if (len > 0)
-          bulk_g2s(reinterpret_cast<unsigned char*>(sh.row) + 512 * RPW * w + 256 * RPW, grow + off,
-                   static_cast<uint32_t>(len), &sh.bar);
-      }
-    } else {
-      bulk_g2s(reinterpret_cast<unsigned char*>(sh.row), grow, row_bytes, &sh.bar);
-    }
+    bulk_g2s(BF16 ? static_cast<void*>(stage) : static_cast<void*>(sh.row), grow, row_bytes, &sh.bar);
   }
 
   // presence scatter from the packed history (RepetitionPenalty's gather
@@ -851,8 +887,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   // the exact x' of entry v (suppress, EOS gate, repetition penalty) and
   // s = x'/T, recomputed from the logits in global memory (L2-resident)
   auto exact_x = [&](int v) -> float {
-    float x = BF16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(grow)[v])
-                   : reinterpret_cast<const float*>(grow)[v];
+    float x = BF16 ? bf16_bits_to_f32(stage[v]) : reinterpret_cast<const float*>(grow)[v];
     if (suppress && suppress[v]) x = NEG_SUPPRESS;
     if (gate && v == eos_id) x = -INFINITY;
     if ((sh.appb[v >> 2] >> (v & 3)) & 1u) x = x > 0.0f ? __fdiv_rn(x, pen) : __fmul_rn(x, pen);
@@ -876,24 +911,14 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   //      whole-vocabulary rows compute s = x'/T here.  Branch-free per entry:
   //      the selects replace data-dependent branches ------------------------
   {
-    // this warp's staged bf16 block (local round i at byte 256 i + 8 l of the
-    // upper half of its region) is read whole before the widened quads
-    // overwrite the region
-    uint2 stq[BF16 ? RPW : 1];
-    if (BF16) {
-      const uint2* stg = reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned char*>(sh.row) +
-                                                        512 * RPW * wi + 256 * RPW);
-#pragma unroll
-      for (int i = 0; i < RPW; ++i) stq[i] = (4 * (lane + 32 * (rb0 + i)) < V) ? stg[lane + 32 * i] : make_uint2(0u, 0u);
-      __syncwarp();
-    }
+    const uint2* stg = reinterpret_cast<const uint2*>(stage);  // bf16 quad h at stg[h]
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
       const int h = lane + 32 * (rb0 + i);
       const bool in = 4 * h < V;
       float v[4];
       if (BF16) {
-        const uint2 q = stq[BF16 ? i : 0];
+        const uint2 q = in ? stg[h] : make_uint2(0u, 0u);
         v[0] = bf16_bits_to_f32(q.x & 0xffffu);
         v[1] = bf16_bits_to_f32(q.x >> 16);
         v[2] = bf16_bits_to_f32(q.y & 0xffffu);
@@ -1182,8 +1207,10 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
           if (cut) {
             // ---- HF TopPLogitsWarper: remove an entry when the mass at or
             //      below it in stable ascending order (s asc, index asc) is
-            //      <= tau = floor((1-p) Zq); the crossing bin's entries are
-            //      resolved exactly, those below it go, those above stay ----
+            //      <= tau = floor((1-p) Zq).  Survivors below the crossing
+            //      bin of the mass histogram go, those above stay; the crossing
+            //      bin's entries are listed (with their masses, in the cleared
+            //      histogram space) and cut exactly among themselves ---------
             const float frac = __fsub_rn(1.0f, top_p);
             if (wi == 0) {
               unsigned long long Zq, tau, before;
@@ -1200,6 +1227,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
             const unsigned long long Zq = sh.selq[0], tau = sh.selq[1], below = sh.selq[2];
             const uint32_t bstar = sh.sel[3];
             const unsigned long long eps = Zq / 1000000ull;
+            unsigned long long* mqs = reinterpret_cast<unsigned long long*>(sh.hist);  // masses of the listed entries
             if (tau >= Zq) {
               // only the ascending-last survivor stays: largest s, then index
               unsigned long long best = 0;
@@ -1214,12 +1242,16 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
             } else {
               for (int p = t; p < n; p += NT) {
                 if (!sh.keep[p]) continue;
-                const float wgt = __uint_as_float(sh.u.cand[p].w);
-                const uint32_t bn = mass_fixed(wgt) ? coarse_bin(wgt) : 0u;
-                if (mass_fixed(wgt) && bn == bstar)
-                  small[atomicAdd(&sh.lcnt[1], 1)] = static_cast<uint8_t>(p);
-                else
-                  kout[p] = mass_fixed(wgt) && bn > bstar;
+                const float wp = __uint_as_float(sh.u.cand[p].w);
+                const unsigned long long qp = mass_fixed(wp);
+                const uint32_t bp = qp ? coarse_bin(wp) : 0u;
+                if (qp && bp == bstar) {
+                  const int slot = atomicAdd(&sh.lcnt[1], 1);
+                  small[slot] = static_cast<uint8_t>(p);
+                  mqs[slot] = qp;
+                } else {
+                  kout[p] = qp && bp > bstar;
+                }
               }
               row_sync<W>();
               const int nc = sh.lcnt[1];
@@ -1231,7 +1263,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
                 for (int k = 0; k < nc; ++k) {
                   const int q = small[k];
                   const float so = __uint_as_float(sh.u.cand[q].x);
-                  if (so < sp || (so == sp && q <= p)) cum += mass_fixed(__uint_as_float(sh.u.cand[q].w));
+                  cum += (so < sp || (so == sp && q <= p)) ? mqs[k] : 0ull;
                 }
                 const bool kp = cum > tau;
                 kout[p] = kp;
