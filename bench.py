@@ -446,7 +446,7 @@ def run_q3s(args):
 
     peak, peak_kind = peaks()
     achieved = bytes_step / (ms_step / 1000) / 1e9
-    traffic = profile_traffic("sample_rows_cfg1_ncu.txt")
+    traffic = profile_traffic("sample_smem_cfg1_ncu.txt")
     clk = clocks.summary(t0, t1)
     if rank == 0:
         line = {
