@@ -83,7 +83,7 @@ Q3S_DEV uint32_t smem_u32(const void* p) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk-copy helpers (no multicast anywhere)
+// mbarrier + bulk-copy helpers (every copy lands in the issuing CTA only)
 // ---------------------------------------------------------------------------
 
 Q3S_DEV void mbar_init(uint64_t* bar, uint32_t count) {
@@ -94,7 +94,7 @@ Q3S_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
-// Plain (non-multicast) bulk copy global -> this CTA's shared memory.
+// Plain bulk copy global -> this CTA's shared memory (one destination).
 Q3S_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -788,7 +788,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   row_sync<W>();
 
   // ---- the row's logits stream into shared memory (bulk copies, no
-  //      multicast), issued by thread 0 after the first barrier (so that no
+  //      single-CTA destination), issued by thread 0 after the first barrier (so that no
   //      other thread waits for the issue) while the history is scattered:
   //      fp32 rows into the row buffer, bf16 rows into their staging buffer
   //      (kept: the exact values of candidates are read back from it) -------
