@@ -198,26 +198,41 @@ Q3S_DEV unsigned long long warp_sum_u64(unsigned long long v) {
 
 // Inverse CDF over a list's kept weights in vocabulary order: the first
 // position whose running sum exceeds u * total.  Lane l owns positions
-// [l P, l P + P), P = ceil(n / 32) -- the association order of the CTA
-// kernels' warp-0 finisher, so both produce the same sums.  The weight of
-// position p = l P + r is wk[r * 32 + l] (transposed: conflict-free loads),
-// 0 for removed entries and for p >= n.
+// [l P, l P + P), P = ceil(n / 32) <= 8 (n <= WCAP) -- the association order
+// of the CTA kernels' warp-0 finisher, so both produce the same sums.  The
+// weight of position p = l P + r is wk[r * 32 + l] (transposed: conflict-free
+// loads), 0 for removed entries and for p >= n.  Each lane reads its weights
+// once, into registers.
 Q3S_DEV int warp_draw_list(const float* wk, int n, float u, int& flags) {
   const int lane = lane_id();
   const int P = (n + 31) / 32;
+  float w[WCAP / 32];
+#pragma unroll
+  for (int r = 0; r < WCAP / 32; ++r) w[r] = r < P ? wk[r * 32 + lane] : 0.0f;
+  // adding the +0 weights past P leaves every sum unchanged
   float a = 0.0f;
-  for (int r = 0; r < P; ++r) a = __fadd_rn(a, wk[r * 32 + lane]);
+#pragma unroll
+  for (int r = 0; r < WCAP / 32; ++r) a = __fadd_rn(a, w[r]);
   float W;
   const float pre = warp_excl_scan_f(a, W);
   const float thr = __fmul_rn(u, W);
+  // cumulative weight through position l P + r: pre + (w_0 + ... + w_r)
   int r_first = -1, r_last = -1;
-  float acc = 0.0f;
-  for (int r = 0; r < P; ++r) {
-    const float w = wk[r * 32 + lane];
-    acc = __fadd_rn(acc, w);
-    if (w > 0.0f) {
+  float part = 0.0f, cdf_f = 0.0f, prev_f = 0.0f, cdf_l = 0.0f, prev_l = 0.0f;
+#pragma unroll
+  for (int r = 0; r < WCAP / 32; ++r) {
+    const float before = __fadd_rn(pre, part);
+    part = __fadd_rn(part, w[r]);
+    const float c = __fadd_rn(pre, part);
+    if (w[r] > 0.0f) {
       r_last = r;
-      if (r_first < 0 && __fadd_rn(pre, acc) > thr) r_first = r;
+      cdf_l = c;
+      prev_l = before;
+      if (r_first < 0 && c > thr) {
+        r_first = r;
+        cdf_f = c;
+        prev_f = before;
+      }
     }
   }
   const unsigned hit = __ballot_sync(FULL, r_first >= 0);
@@ -231,17 +246,9 @@ Q3S_DEV int warp_draw_list(const float* wk, int n, float u, int& flags) {
     rsel = any ? __shfl_sync(FULL, r_last, src) : 0;
     flags |= Q3S_ROW_FALLBACK;
   }
-  int near = 0;
-  if (lane == src) {
-    float cdf = pre, prev = pre, a2 = 0.0f;
-    for (int r = 0; r <= rsel; ++r) {
-      a2 = __fadd_rn(a2, wk[r * 32 + lane]);
-      if (r < rsel) prev = __fadd_rn(pre, a2);
-      cdf = __fadd_rn(pre, a2);
-    }
-    const float tol = BOUNDARY_EPS * W;
-    near = (__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol);
-  }
+  const float cdf = hit ? cdf_f : cdf_l, prev = hit ? prev_f : prev_l;
+  const float tol = BOUNDARY_EPS * W;
+  const int near = (__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol);
   if (__shfl_sync(FULL, near, src)) flags |= Q3S_ROW_DRAW_BOUNDARY;
   return src * P + rsel;
 }
@@ -391,7 +398,7 @@ struct alignas(16) RowSmem {
     uint4 cand[WCAP];                    // candidate records {s bits, index, x' bits, weight bits}
     float ex[32 * RQ];                   // draw: cumulative weight before each quad, within its warp's block
   } u;
-  uint8_t appb[32 * RQ];                 // presence bits of quad h (low 4 bits)
+  uint8_t appb[32 * RQ];                 // quad h: presence bits (low 4), suppress bits (high 4)
   uint8_t cmask[32 * RQ];                // candidate bits of quad h (low 4 bits)
   uint8_t keep[WCAP];
   float xf[2][W];                        // cross-warp exchange, double-buffered
@@ -778,19 +785,10 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     const int h = lane + 32 * (rb0 + i);
     supw[i] = (suppress && 4 * h < V) ? __ldg(reinterpret_cast<const uint32_t*>(suppress + 4 * h)) : 0u;
   }
-  {
-    // zero the histograms and the presence flags
-    uint4* hz = reinterpret_cast<uint4*>(&sh.hist[0][0]);
-    for (int i = t; i < 2 * NBINS / 4; i += NT) hz[i] = make_uint4(0, 0, 0, 0);
-    uint4* sz = reinterpret_cast<uint4*>(sh.u.seen);
-    for (int i = t; i < Smem::VMAX / 16; i += NT) sz[i] = make_uint4(0, 0, 0, 0);
-  }
-  row_sync<W>();
-
-  // ---- the row's logits stream into shared memory (bulk copies, no
-  //      single-CTA destination), issued by thread 0 after the first barrier (so that no
-  //      other thread waits for the issue) while the history is scattered:
-  //      fp32 rows into the row buffer, bf16 rows into their staging buffer
+  // ---- the row's logits stream into shared memory (one plain bulk copy
+  //      into this CTA's memory, issued before anything else so that it
+  //      overlaps the parameter loads and the history scatter): fp32 rows
+  //      straight into the row buffer, bf16 rows into their staging buffer
   //      (kept: the exact values of candidates are read back from it) -------
   if (t == 0) {
     mbar_init(&sh.bar, 1);
@@ -798,6 +796,14 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     mbar_expect_tx(&sh.bar, row_bytes);
     bulk_g2s(BF16 ? static_cast<void*>(stage) : static_cast<void*>(sh.row), grow, row_bytes, &sh.bar);
   }
+  {
+    // zero the histograms and the presence flags (the copy writes neither)
+    uint4* hz = reinterpret_cast<uint4*>(&sh.hist[0][0]);
+    for (int i = t; i < 2 * NBINS / 4; i += NT) hz[i] = make_uint4(0, 0, 0, 0);
+    uint4* sz = reinterpret_cast<uint4*>(sh.u.seen);
+    for (int i = t; i < Smem::VMAX / 16; i += NT) sz[i] = make_uint4(0, 0, 0, 0);
+  }
+  row_sync<W>();
 
   // presence scatter from the packed history (RepetitionPenalty's gather
   // set); racing stores of the same byte need no atomics
@@ -888,9 +894,10 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   // s = x'/T, recomputed from the logits in global memory (L2-resident)
   auto exact_x = [&](int v) -> float {
     float x = BF16 ? bf16_bits_to_f32(stage[v]) : reinterpret_cast<const float*>(grow)[v];
-    if (suppress && suppress[v]) x = NEG_SUPPRESS;
+    const uint32_t ab = sh.appb[v >> 2] >> (v & 3);
+    if ((ab >> 4) & 1u) x = NEG_SUPPRESS;
     if (gate && v == eos_id) x = -INFINITY;
-    if ((sh.appb[v >> 2] >> (v & 3)) & 1u) x = x > 0.0f ? __fdiv_rn(x, pen) : __fmul_rn(x, pen);
+    if (ab & 1u) x = x > 0.0f ? __fdiv_rn(x, pen) : __fmul_rn(x, pen);
     return x;
   };
   auto exact_s = [&](int v) -> float {
@@ -937,7 +944,9 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         for (int j = 0; j < 4; ++j) {
           const bool ap = ((f >> (8 * j)) & 0xffu) != 0u;
           app |= (ap ? 1u : 0u) << j;
-          float x = ((supw[i] >> (8 * j)) & 0xffu) ? NEG_SUPPRESS : v[j];
+          const bool sup = ((supw[i] >> (8 * j)) & 0xffu) != 0u;
+          app |= (sup ? 16u : 0u) << j;
+          float x = sup ? NEG_SUPPRESS : v[j];
           x = (gate && 4 * h + j == eos_id) ? -INFINITY : x;
           if (cand_path) {
             // the approximate value: x * pen for present entries <= 0 (exact),
@@ -1080,7 +1089,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     // past the exchange every warp is done with the histograms: zero them
     for (int i = t; i < 2 * NBINS; i += NT) (&sh.hist[0][0])[i] = 0u;
     if (n <= WCAP) {
-      // records {0, index, 0, 0}; the list's first step fills in x' and s
+      // records {0, index, 0, 0}; the list's next step fills in x' and s
 #pragma unroll 2
       for (int r = rb0; r < rb1; ++r) {
         const int h = lane + 32 * r;
@@ -1098,20 +1107,29 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     }
     row_sync<W>();
     if (n <= WCAP) {
-      // ---- the list, all threads: exact x' (recomputed from the logits in
-      //      L2, one load round trip for all candidates at once) and s per
-      //      candidate; padding records never outrank and weigh nothing -------
+      // ---- the list, all threads: exact x' (recomputed from the staged row
+      //      or L2, one load round trip for all candidates at once) and s per
+      //      candidate, s again by position in the row buffer (dead past the
+      //      compaction; NaN padding never compares), the list's maximum and
+      //      the proof window -- one exchange -------------------------------
+      float* sf = rowf;
+      float m = -INFINITY, bad = 0.0f;
       for (int p = t; p < n4; p += NT) {
         if (p < n) {
           const uint32_t v = sh.u.cand[p].y;
           const float x = exact_x(static_cast<int>(v));
           const float s = greedy ? x : __fdiv_rn(x, T);
           sh.u.cand[p] = make_uint4(__float_as_uint(s), v, __float_as_uint(x), 0u);
+          sf[p] = s;
+          m = fmaxf(m, s);
+          const float ap = fabsf(s);
+          bad = (ap >= 0x1p-100f && ap <= 0x1p100f) ? bad : 1.0f;
         } else {
-          sh.u.cand[p] = make_uint4(0xff800000u, 0x7fffffffu, 0xff800000u, 0u);
+          sf[p] = __int_as_float(0x7fc00000);
         }
       }
-      row_sync<W>();
+      X.max2_f(m, bad);
+      if (W == 1) __syncwarp();
       if (greedy) {
         // argmax of x' (torch.argmax order: lowest index on ties)
         float bv = -INFINITY;
@@ -1128,157 +1146,117 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         id = bi;
         flags = Q3S_ROW_GREEDY;
         done = true;
-      } else {
-        // The list's maximum and the proof window (below) by one exchange.
-        float m = -INFINITY, bad = 0.0f;
-        for (int p = t; p < n; p += NT) {
-          const float sp = __uint_as_float(sh.u.cand[p].x);
-          m = fmaxf(m, sp);
-          const float ap = fabsf(sp);
-          bad = (ap >= 0x1p-100f && ap <= 0x1p100f) ? bad : 1.0f;
-        }
-        X.max2_f(m, bad);
-        // quotients far from 1 may merge more than 40 key units of x' (or
-        // more than one fine bin): the candidate set is proven complete only
-        // while every candidate's |s| stays inside this window
-        if (m != -INFINITY && bad == 0.0f) {
-          uint8_t* kout = sh.cmask;        // kept entries (positions < 256)
-          uint8_t* small = sh.cmask + 256; // short index lists (positions)
-          if (t == 0) {
-            sh.res[3] = 0;
-            sh.lcnt[0] = 0;
-            sh.lcnt[1] = 0;
+      } else if (m != -INFINITY && bad == 0.0f) {
+        // Quotients far from 1 may merge more than one fine bin (or 40 key
+        // units) of x': the candidate set is proven complete only while
+        // every candidate's |s| stays inside the window checked above.
+        //
+        // ---- exact order by all pairs: per candidate, how many s are below
+        //      it and at or below it (L lanes split the list).  HF TopK keeps
+        //      s >= the K-th largest (ties kept): fewer than K strictly
+        //      above.  The stable ascending slot (s asc, index asc) of a kept
+        //      entry orders HF TopP's cumulative masses; entries TopK drops
+        //      take the lowest slots (they are strictly below every kept one)
+        //      and weigh nothing.  Kept softmax weights go to the draw's
+        //      transposed layout; with top-p, exact fixed-point masses and
+        //      positions by ascending slot -----------------------------------
+        const bool cut = top_p < 1.0f;
+        const int L = list_lanes(n4, NT);
+        const int P = (n + 31) >> 5;
+        float* wk = reinterpret_cast<float*>(sh.hist);                                 // 32 P <= 256
+        unsigned long long* mqa = reinterpret_cast<unsigned long long*>(rowf + WCAP);  // by ascending slot
+        uint8_t* asca = sh.cmask;                                                      // slot by position
+        const float4* sf4 = reinterpret_cast<const float4*>(sf);
+        const int sl = lane % L;
+        for (int pw = (t - lane) / L; pw < 32 * P; pw += NT / L) {
+          const int p = pw + lane / L;  // warp-uniform trip count: every lane shuffles
+          const bool act = p < n;
+          const float sp = act ? sf[p] : __int_as_float(0x7fc00000);
+          // below: s < sp; at or below: s <= sp; equal s at lower positions
+          // (quads wholly before p: at-or-below minus below; p's own quad:
+          // the entries before it)
+          const int p4 = p >> 2, pj = p & 3;
+          int lt = 0, le = 0, eb = 0;
+          for (int q4 = sl; q4 < (n4 >> 2); q4 += L) {
+            const float4 f = sf4[q4];
+            const int cl = (f.x < sp) + (f.y < sp) + (f.z < sp) + (f.w < sp);
+            const int ce = (f.x <= sp) + (f.y <= sp) + (f.z <= sp) + (f.w <= sp);
+            lt += cl;
+            le += ce;
+            if (q4 < p4) eb += ce - cl;
+            if (q4 == p4) eb += (pj > 0 && f.x == sp) + (pj > 1 && f.y == sp) + (pj > 2 && f.z == sp);
           }
-          row_sync<W>();
-          // ---- HF TopK keeps s >= the K-th largest s (ties kept) ------------
-          if (linear) {
-            // Candidates two fine bins or more above the K-th largest's bin
-            // beat it in exact s (the bins are far wider than the error
-            // window): they survive.  The rest -- the band of fine bins
-            // bb-1 .. bb+1 -- hold the K-th largest as their (K - above)-th
-            // largest; exact ranks there.
-            const float dband = __fadd_rn(dcut, static_cast<float>(static_cast<int>(bb) - 2) * (1.0f / 64.0f));
-            for (int p = t; p < n; p += NT) {
-              const float d = dist(rowf[sh.u.cand[p].y]);
-              const bool inb = d >= dband;
-              sh.keep[p] = !inb;
-              if (inb) small[atomicAdd(&sh.lcnt[0], 1)] = static_cast<uint8_t>(p);
-            }
-            row_sync<W>();
-            const int nb = sh.lcnt[0];
-            const int kb = K - (n - nb);  // rank of the K-th inside the band
-            for (int i = t; i < nb; i += NT) {
-              const int p = small[i];
-              const float sp = __uint_as_float(sh.u.cand[p].x);
-              int above = 0;
-              for (int k = 0; k < nb; ++k) above += __uint_as_float(sh.u.cand[small[k]].x) > sp;
-              sh.keep[p] = above < kb;
-            }
-          } else {
-            // radix-selected candidates: exact all-pairs ranks
-            for (int p = t; p < n; p += NT) {
-              const float sp = __uint_as_float(sh.u.cand[p].x);
-              int above = 0;
-              for (int q = 0; q < n; ++q) above += __uint_as_float(sh.u.cand[q].x) > sp;
-              sh.keep[p] = above < K;
-            }
+          for (int o = 1; o < L; o <<= 1) {
+            lt += __shfl_xor_sync(FULL, lt, o);
+            le += __shfl_xor_sync(FULL, le, o);
+            eb += __shfl_xor_sync(FULL, eb, o);
           }
-          row_sync<W>();
-          // softmax weights of the survivors; with top-p, their exact
-          // fixed-point masses into the coarse histogram (by the weight's
-          // exponent and top mantissa bits, monotone in s)
-          const bool cut = top_p < 1.0f;
-          constexpr uint32_t LO = (1u << MASS_LO_BITS) - 1u;
-          for (int p = t; p < n; p += NT) {
-            const bool sv = sh.keep[p];
-            const float wgt = sv ? softmax_weight(__uint_as_float(sh.u.cand[p].x), m) : 0.0f;
-            sh.u.cand[p].w = __float_as_uint(wgt);
-            kout[p] = sv;
-            if (cut && sv) {
-              const unsigned long long q = mass_fixed(wgt);
-              if (q) {
-                const uint32_t bn = coarse_bin(wgt);
-                atomicAdd(&sh.hist[0][bn], static_cast<uint32_t>(q >> MASS_LO_BITS));
-                atomicAdd(&sh.hist[1][bn], static_cast<uint32_t>(q) & LO);
+          if (sl == 0) {
+            float w = 0.0f;
+            if (act) {
+              const int asc = lt + eb;
+              w = n - le < K ? softmax_weight(sp, m) : 0.0f;
+              if (cut) {
+                mqa[asc] = mass_fixed(w);
+                asca[p] = static_cast<uint8_t>(asc);
               }
             }
+            wk[(p % P) * 32 + p / P] = w;
           }
-          row_sync<W>();
+        }
+        row_sync<W>();
+        // ---- warp 0 alone from here: top-p over the ascending slots, the
+        //      draw over positions (vocabulary order) ------------------------
+        if (wi == 0) {
+          int lflags = 0;
           if (cut) {
-            // ---- HF TopPLogitsWarper: remove an entry when the mass at or
-            //      below it in stable ascending order (s asc, index asc) is
-            //      <= tau = floor((1-p) Zq).  Survivors below the crossing
-            //      bin of the mass histogram go, those above stay; the crossing
-            //      bin's entries are listed (with their masses, in the cleared
-            //      histogram space) and cut exactly among themselves ---------
+            // HF TopPLogitsWarper: slot i goes when the mass of slots <= i is
+            // <= tau = floor((1-p) Zq); the last slot stays
             const float frac = __fsub_rn(1.0f, top_p);
-            if (wi == 0) {
-              unsigned long long Zq, tau, before;
-              uint32_t bstar;
-              warp_scan_mass_total(sh.hist[0], sh.hist[1], frac, Zq, tau, bstar, before);
-              if (lane == 0) {
-                sh.selq[0] = Zq;
-                sh.selq[1] = tau;
-                sh.selq[2] = before;
-                sh.sel[3] = bstar;
-              }
+            const int i0 = 8 * lane;
+            unsigned long long c[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              c[j] = i0 + j < n ? mqa[i0 + j] : 0ull;
+              sum += c[j];
             }
-            row_sync<W>();
-            const unsigned long long Zq = sh.selq[0], tau = sh.selq[1], below = sh.selq[2];
-            const uint32_t bstar = sh.sel[3];
+            unsigned long long inc = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const unsigned long long y = __shfl_up_sync(FULL, inc, o);
+              if (lane >= o) inc += y;
+            }
+            const unsigned long long Zq = __shfl_sync(FULL, inc, 31);
+            const unsigned long long tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
             const unsigned long long eps = Zq / 1000000ull;
-            unsigned long long* mqs = reinterpret_cast<unsigned long long*>(sh.hist);  // masses of the listed entries
-            if (tau >= Zq) {
-              // only the ascending-last survivor stays: largest s, then index
-              unsigned long long best = 0;
-              for (int p = t; p < n; p += NT)
-                if (sh.keep[p]) {
-                  const unsigned long long key =
-                      (static_cast<unsigned long long>(f2key(__uint_as_float(sh.u.cand[p].x))) << 32) | p;
-                  best = key > best ? key : best;
-                }
-              best = X.max_q(best);
-              for (int p = t; p < n; p += NT) kout[p] = sh.keep[p] && p == static_cast<int>(best & 0xffffffffu);
-            } else {
-              for (int p = t; p < n; p += NT) {
-                if (!sh.keep[p]) continue;
-                const float wp = __uint_as_float(sh.u.cand[p].w);
-                const unsigned long long qp = mass_fixed(wp);
-                const uint32_t bp = qp ? coarse_bin(wp) : 0u;
-                if (qp && bp == bstar) {
-                  const int slot = atomicAdd(&sh.lcnt[1], 1);
-                  small[slot] = static_cast<uint8_t>(p);
-                  mqs[slot] = qp;
-                } else {
-                  kout[p] = qp && bp > bstar;
-                }
-              }
-              row_sync<W>();
-              const int nc = sh.lcnt[1];
-              bool near = t == 0 && tau - below < eps;
-              for (int i = t; i < nc; i += NT) {
-                const int p = small[i];
-                const float sp = __uint_as_float(sh.u.cand[p].x);
-                unsigned long long cum = below;
-                for (int k = 0; k < nc; ++k) {
-                  const int q = small[k];
-                  const float so = __uint_as_float(sh.u.cand[q].x);
-                  cum += (so < sp || (so == sp && q <= p)) ? mqs[k] : 0ull;
-                }
-                const bool kp = cum > tau;
-                kout[p] = kp;
-                near |= kp ? (cum - tau < eps) : (tau - cum < eps);
-              }
-              if (near) atomicOr(&sh.res[3], Q3S_ROW_TOPP_BOUNDARY);
+            // the removed slots are a prefix (cumulative masses only grow):
+            // icut of them; this lane's positions below it weigh nothing
+            unsigned long long cum = inc - sum;
+            bool near = false;
+            int below = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int i = i0 + j;
+              cum += c[j];
+              const bool last = i >= n - 1;
+              below += !last && cum <= tau;
+              if (c[j] && !last && tau < Zq) near |= cum > tau ? (cum - tau < eps) : (tau - cum < eps);
             }
-            row_sync<W>();
-            flags |= sh.res[3];
+            const int icut = __reduce_add_sync(FULL, static_cast<unsigned>(below));
+            if (__any_sync(FULL, near)) lflags |= Q3S_ROW_TOPP_BOUNDARY;
+            int sa[WCAP / 32];
+#pragma unroll
+            for (int r = 0; r < WCAP / 32; ++r) sa[r] = r < P && lane * P + r < n ? asca[lane * P + r] : WCAP;
+#pragma unroll
+            for (int r = 0; r < WCAP / 32; ++r)
+              if (sa[r] < icut) wk[r * 32 + lane] = 0.0f;
+            __syncwarp();
           }
-          const int pos = row_draw_list<R, W>(sh, kout, reinterpret_cast<float*>(sh.hist), n, u);
+          const int pos = warp_draw_list(wk, n, u, lflags);
           id = static_cast<int>(sh.u.cand[pos].y);
-          flags |= sh.res[1];
-          done = true;
+          flags = lflags;
         }
+        done = true;
       }
     }
     if (!done) {
