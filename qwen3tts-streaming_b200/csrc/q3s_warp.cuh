@@ -199,16 +199,15 @@ Q3S_DEV unsigned long long warp_sum_u64(unsigned long long v) {
 // Inverse CDF over a list's kept weights in vocabulary order: the first
 // position whose running sum exceeds u * total.  Lane l owns positions
 // [l P, l P + P), P = ceil(n / 32) <= 8 (n <= WCAP) -- the association order
-// of the CTA kernels' warp-0 finisher, so both produce the same sums.  The
-// weight of position p = l P + r is wk[r * 32 + l] (transposed: conflict-free
-// loads), 0 for removed entries and for p >= n.  Each lane reads its weights
-// once, into registers.
+// of the CTA kernels' warp-0 finisher, so both produce the same sums.  wk[p]
+// is the weight of position p, 0 for removed entries and for n <= p < 32 P.
+// Each lane reads its weights once, into registers.
 Q3S_DEV int warp_draw_list(const float* wk, int n, float u, int& flags) {
   const int lane = lane_id();
   const int P = (n + 31) / 32;
   float w[WCAP / 32];
 #pragma unroll
-  for (int r = 0; r < WCAP / 32; ++r) w[r] = r < P ? wk[r * 32 + lane] : 0.0f;
+  for (int r = 0; r < WCAP / 32; ++r) w[r] = r < P ? wk[lane * P + r] : 0.0f;
   // adding the +0 weights past P leaves every sum unchanged
   float a = 0.0f;
 #pragma unroll
@@ -251,14 +250,6 @@ Q3S_DEV int warp_draw_list(const float* wk, int n, float u, int& flags) {
   const int near = (__fsub_rn(cdf, thr) < tol) || (__fsub_rn(thr, prev) < tol);
   if (__shfl_sync(FULL, near, src)) flags |= Q3S_ROW_DRAW_BOUNDARY;
   return src * P + rsel;
-}
-
-// Lanes per candidate for a list of n4 entries and NT threads: the largest
-// power of two <= NT / n4, at most 8 (at least 1).
-Q3S_DEV int list_lanes(int n4, int nt) {
-  int tp = 1;
-  while (tp < 8 && 2 * tp * max(n4, 1) <= nt) tp *= 2;
-  return tp;
 }
 
 // Exclusive prefix over the lanes of a small count (0..7) and the warp total,
@@ -715,7 +706,7 @@ Q3S_DEV int row_draw_list(RowSmem<R, W>& sh, const uint8_t* kout, float* wk, int
   const int t = static_cast<int>(threadIdx.x);
   const int P = (n + 31) / 32;
   for (int p = t; p < 32 * P; p += 32 * W)
-    wk[(p % P) * 32 + p / P] = (p < n && kout[p]) ? __uint_as_float(sh.u.cand[p].w) : 0.0f;
+    wk[p] = (p < n && kout[p]) ? __uint_as_float(sh.u.cand[p].w) : 0.0f;
   row_sync<W>();
   if (t < 32) {
     int lflags = 0;
@@ -868,8 +859,9 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
   const bool cand_path = few && window_ok;
   const bool divT = !greedy && T != 1.0f;  // x / 1 == x exactly
 
-  // the presence flags are complete and the mbarrier is initialised; every
-  // thread waits for the row (bounded) and all see the same outcome
+  // the presence flags are complete (the mbarrier's initialisation was
+  // published by the first barrier); every thread waits for the row
+  // (bounded) and all see the same outcome
   row_sync<W>();
   const bool arrived = mbar_wait_bounded(&sh.bar, 0);
   bool all_arrived;
@@ -979,19 +971,21 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
     //      instead of x / pen for present entries > 0, within 2 ulps); select
     //      a threshold on them, resolve exactly on the candidates ------------
     //
-    // Two histograms of d = max - value: bins 1 wide over d < 255, then bins
-    // 1/64 wide over the two unit bins from the one holding the K-th largest.
-    // With every value in [-2000, 2000] an ulp is <= 2^-12, so the
-    // approximation error plus any temperature-tie window (a few ulps) stays
-    // far inside one fine bin: every entry above the fine bin holding the
-    // K-th largest, in it, or in the next one down is a candidate.  Otherwise
+    // Histograms of d = max - value: bins 1/8 wide over d < 32 when that
+    // locates the K-th largest tightly enough, else bins 1 wide over d < 255
+    // and then bins 1/64 wide over the two unit bins from the one holding the
+    // K-th largest.  With every value in [-2000, 2000] an ulp is <= 2^-12, so
+    // the approximation error plus any temperature-tie window (a few ulps)
+    // stays far inside one bin: every entry above the bin holding the K-th
+    // largest, in it, or in the next one down is a candidate.  Otherwise
     // (wider values, NaN, the K-th below d = 253) a radix select on the
     // approximate keys with a 40-unit margin.
     amax = X.max_f(anan ? INFINITY : amax);
     auto dist = [&](float v) -> float { return __fsub_rn(amax, v); };
     bool linear = fabsf(amax) <= 2000.0f;
-    uint32_t ba = 0, bb = 0;  // unit bin and fine bin of the K-th largest
-    if (linear) {
+    // counts of the entries with (d - d0) * scale in [0, lim), by bin
+    // 255 - floor((d - d0) * scale) (the scans run from the top down)
+    auto bin_pass = [&](uint32_t* hist, float d0, float scale, float lim) {
 #pragma unroll 2
       for (int r = rb0; r < rb1; ++r) {
         const int h = lane + 32 * r;
@@ -1000,36 +994,50 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         const float v[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float d = dist(v[j]);
-          if (d < 255.0f) atomicAdd(&sh.hist[0][255u - static_cast<uint32_t>(d)], 1u);
+          const float e = __fmul_rn(__fsub_rn(dist(v[j]), d0), scale);
+          if (e >= 0.0f && e < lim) atomicAdd(&hist[255u - static_cast<uint32_t>(e)], 1u);
         }
       }
+    };
+    // candidates: d < dcut, or (d - dcut) * dsc < ecut
+    float dcut = 0.0f, dsc = 8.0f, ecut = 0.0f;
+    if (linear) {
+      // Bins 1/8 wide over d < 32: when the K-th largest lies there and the
+      // entries down to the bin below its own number at most WCAP, they are
+      // the candidates.  Every warp scans the histogram itself (no
+      // broadcast) and reaches the same decision.
+      bin_pass(sh.hist[0], 0.0f, 8.0f, 256.0f);
       row_sync<W>();
-      // every warp scans the histogram itself (no broadcast)
-      uint32_t da, krem;
-      warp_scan_count_desc_keep(sh.hist[0], static_cast<uint32_t>(K), da, krem);
-      ba = 255u - da;
-      linear = ba <= 253u;
-      if (linear) {
-        const float d0 = static_cast<float>(ba);
-#pragma unroll 2
-        for (int r = rb0; r < rb1; ++r) {
-          const int h = lane + 32 * r;
-          if (4 * h >= V) continue;
-          const float4 q = sh.row[h];
-          const float v[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float e = __fmul_rn(__fsub_rn(dist(v[j]), d0), 64.0f);
-            if (e >= 0.0f && e < 128.0f) atomicAdd(&sh.hist[1][255u - static_cast<uint32_t>(e)], 1u);
-          }
-        }
+      uint32_t d8, k8;
+      warp_scan_count_desc_keep(sh.hist[0], static_cast<uint32_t>(K), d8, k8);
+      const uint32_t b8 = 255u - d8;
+      uint32_t n8 = WCAP + 1;
+      if (b8 <= 253u) n8 = (static_cast<uint32_t>(K) - k8) + sh.hist[0][255u - b8] + sh.hist[0][254u - b8];
+      if (n8 <= static_cast<uint32_t>(WCAP)) {
+        ecut = static_cast<float>(b8 + 2u);
+      } else {
+        // Otherwise bins 1 wide over d < 255, then bins 1/64 wide over the
+        // two unit bins from the one holding the K-th largest.
         row_sync<W>();
-        uint32_t db, kb;
-        warp_scan_count_desc_keep(sh.hist[1], krem, db, kb);
-        bb = 255u - db;
+        for (int i = t; i < NBINS; i += NT) sh.hist[0][i] = 0u;
+        row_sync<W>();
+        bin_pass(sh.hist[0], 0.0f, 1.0f, 255.0f);
+        row_sync<W>();
+        uint32_t da, krem;
+        warp_scan_count_desc_keep(sh.hist[0], static_cast<uint32_t>(K), da, krem);
+        const uint32_t ba = 255u - da;
+        linear = ba <= 253u;
+        if (linear) {
+          bin_pass(sh.hist[1], static_cast<float>(ba), 64.0f, 128.0f);
+          row_sync<W>();
+          uint32_t db, kb;
+          warp_scan_count_desc_keep(sh.hist[1], krem, db, kb);
+          dcut = static_cast<float>(ba);
+          dsc = 64.0f;
+          ecut = static_cast<float>(255u - db + 2u);  // fine bins <= the K-th's + 1
+        }
       }
-      // every warp has read both histograms once all pass the compaction's
+      // every warp has read the histograms once all pass the compaction's
       // exchange below; the histograms are cleared after it
     }
     uint32_t lo = 0;
@@ -1055,8 +1063,6 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
       lo = thr > 40u ? thr - 40u : 0u;
     }
     // candidates: masks per quad, then records in vocabulary order
-    const float dcut = static_cast<float>(ba);
-    const float ecut = static_cast<float>(bb + 2u);  // fine bins <= bb + 1
     uint32_t cnt = 0;
 #pragma unroll 2
     for (int r = rb0; r < rb1; ++r) {
@@ -1070,7 +1076,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
           bool c;
           if (linear) {
             const float d = dist(v[j]);
-            c = d < dcut || __fmul_rn(__fsub_rn(d, dcut), 64.0f) < ecut;
+            c = d < dcut || __fmul_rn(__fsub_rn(d, dcut), dsc) < ecut;
           } else {
             c = f2key(v[j]) >= lo;
           }
@@ -1151,58 +1157,60 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
         // units) of x': the candidate set is proven complete only while
         // every candidate's |s| stays inside the window checked above.
         //
-        // ---- exact order by all pairs: per candidate, how many s are below
-        //      it and at or below it (L lanes split the list).  HF TopK keeps
-        //      s >= the K-th largest (ties kept): fewer than K strictly
-        //      above.  The stable ascending slot (s asc, index asc) of a kept
+        // ---- exact order by all pairs: per candidate (LP threads each, the
+        //      list split between them), its stable ascending slot (s asc,
+        //      index asc); the entry in slot n - K is the K-th largest, and
+        //      HF TopK keeps s >= it (ties kept).  The slot of a kept
         //      entry orders HF TopP's cumulative masses; entries TopK drops
         //      take the lowest slots (they are strictly below every kept one)
-        //      and weigh nothing.  Kept softmax weights go to the draw's
-        //      transposed layout; with top-p, exact fixed-point masses and
-        //      positions by ascending slot -----------------------------------
+        //      and weigh nothing.  Kept softmax weights by position for the
+        //      draw; with top-p, exact fixed-point masses by ascending slot
+        //      and the slot of each position ---------------------------------
         const bool cut = top_p < 1.0f;
-        const int L = list_lanes(n4, NT);
         const int P = (n + 31) >> 5;
         float* wk = reinterpret_cast<float*>(sh.hist);                                 // 32 P <= 256
         unsigned long long* mqa = reinterpret_cast<unsigned long long*>(rowf + WCAP);  // by ascending slot
         uint8_t* asca = sh.cmask;                                                      // slot by position
         const float4* sf4 = reinterpret_cast<const float4*>(sf);
-        const int sl = lane % L;
-        for (int pw = (t - lane) / L; pw < 32 * P; pw += NT / L) {
-          const int p = pw + lane / L;  // warp-uniform trip count: every lane shuffles
+        constexpr int LP = W >= 16 ? 4 : (W >= 8 ? 2 : 1);
+        const int sl = t & (LP - 1);
+        float* skth = reinterpret_cast<float*>(&sh.sel[0]);  // the K-th largest s
+        for (int pb = 0; pb < 32 * P; pb += NT / LP) {
+          // the ascending slot of p: entries below it, counting equal s at
+          // lower positions -- s <= sp in quads wholly before p's (s < spu,
+          // spu the next float up: every |s| here is normal and finite),
+          // s < sp elsewhere, then p's own quad's earlier equal entries
+          const int p = pb + t / LP;  // warp-uniform trip count: every lane shuffles
           const bool act = p < n;
           const float sp = act ? sf[p] : __int_as_float(0x7fc00000);
-          // below: s < sp; at or below: s <= sp; equal s at lower positions
-          // (quads wholly before p: at-or-below minus below; p's own quad:
-          // the entries before it)
-          const int p4 = p >> 2, pj = p & 3;
-          int lt = 0, le = 0, eb = 0;
-          for (int q4 = sl; q4 < (n4 >> 2); q4 += L) {
+          const float spu = __uint_as_float(__float_as_uint(sp) + (sp > 0.0f ? 1u : 0xffffffffu));
+          const int p4 = p >> 2;
+          int c = 0;
+#pragma unroll 4
+          for (int q4 = sl; q4 < (n4 >> 2); q4 += LP) {
             const float4 f = sf4[q4];
-            const int cl = (f.x < sp) + (f.y < sp) + (f.z < sp) + (f.w < sp);
-            const int ce = (f.x <= sp) + (f.y <= sp) + (f.z <= sp) + (f.w <= sp);
-            lt += cl;
-            le += ce;
-            if (q4 < p4) eb += ce - cl;
-            if (q4 == p4) eb += (pj > 0 && f.x == sp) + (pj > 1 && f.y == sp) + (pj > 2 && f.z == sp);
+            const float th = q4 < p4 ? spu : sp;
+            c += (f.x < th) + (f.y < th) + (f.z < th) + (f.w < th);
           }
-          for (int o = 1; o < L; o <<= 1) {
-            lt += __shfl_xor_sync(FULL, lt, o);
-            le += __shfl_xor_sync(FULL, le, o);
-            eb += __shfl_xor_sync(FULL, eb, o);
+#pragma unroll
+          for (int o = 1; o < LP; o <<= 1) c += __shfl_xor_sync(FULL, c, o);
+          if (act && sl == 0) {
+            for (int j = 4 * p4; j < p; ++j) c += sf[j] == sp;
+            asca[p] = static_cast<uint8_t>(c);
+            if (c == n - K) *skth = sp;  // ascending slot n - K: the K-th largest
           }
-          if (sl == 0) {
-            float w = 0.0f;
-            if (act) {
-              const int asc = lt + eb;
-              w = n - le < K ? softmax_weight(sp, m) : 0.0f;
-              if (cut) {
-                mqa[asc] = mass_fixed(w);
-                asca[p] = static_cast<uint8_t>(asc);
-              }
-            }
-            wk[(p % P) * 32 + p / P] = w;
+        }
+        row_sync<W>();
+        // kept by TopK: s >= the K-th largest (ties kept)
+        const float sK = *skth;
+        for (int p = t; p < 32 * P; p += NT) {
+          float w = 0.0f;
+          if (p < n) {
+            const float sp = sf[p];
+            w = sp >= sK ? softmax_weight(sp, m) : 0.0f;
+            if (cut) mqa[asca[p]] = mass_fixed(w);
           }
+          wk[p] = w;
         }
         row_sync<W>();
         // ---- warp 0 alone from here: top-p over the ascending slots, the
@@ -1249,7 +1257,7 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
             for (int r = 0; r < WCAP / 32; ++r) sa[r] = r < P && lane * P + r < n ? asca[lane * P + r] : WCAP;
 #pragma unroll
             for (int r = 0; r < WCAP / 32; ++r)
-              if (sa[r] < icut) wk[r * 32 + lane] = 0.0f;
+              if (sa[r] < icut) wk[lane * P + r] = 0.0f;
             __syncwarp();
           }
           const int pos = warp_draw_list(wk, n, u, lflags);

@@ -497,3 +497,29 @@ def test_warp_kernel_bad_history_is_reported(cuda_device, q3s_lib, policy):
     hist = [np.array([5, 3000, -1], np.int32), np.array([7], np.int32)]
     _, _, err, _ = _warp_case(cuda_device, x, policy=policy, hist=hist)
     assert err & _lib.DEVERR_HISTORY_ID
+
+
+@pytest.mark.parametrize("policy", WARP_POLICIES)
+@pytest.mark.parametrize("bf16", [False, True])
+def test_warp_kernel_threshold_paths(cuda_device, q3s_lib, policy, bf16):
+    """Rows that take each way of locating the K-th largest in the row kernel:
+    bins 1/8 wide near the top, unit bins then 1/64 bins (the K-th 32 or more
+    below the top, or too many entries near it for 1/8 bins), the radix
+    select (values beyond +-2000), and the exact whole-row path."""
+    rng = np.random.default_rng(21)
+    V = 3072
+    x = (rng.standard_normal((10, V)) * 3).astype(np.float32)   # rows 0-1: 1/8 bins
+    x[2] = rng.standard_normal(V)
+    x[2, 11] = 60.0                                             # K-th ~60 below the top
+    x[3] = rng.standard_normal(V) * 0.1                         # dense: 1/64 bins needed
+    x[4] = rng.standard_normal(V) * 0.1 + 500.0                 # dense, offset
+    x[5] = rng.standard_normal(V) * 0.004                       # denser still: exact path
+    x[6] = rng.standard_normal(V) * 1000.0                      # beyond +-2000: radix select
+    x[7, :40] = -1e9                                            # a suppressed block at the top positions
+    x[8] = np.round(rng.standard_normal(V) * 8) / 8             # many exact ties on the 1/8 grid
+    x[9] = rng.standard_normal(V) * 20.0                        # wide spread
+    T = np.array([0.7, 1.3, 0.9, 0.9, 0.9, 0.9, 0.9, 0.8, 0.9, 1.0], np.float32)
+    for k, p in ((20, 1.0), (50, 0.9), (100, 0.95), (128, 0.8)):
+        ids, kf, err, ref = _warp_case(cuda_device, x, bf16=bf16, policy=policy, T=T, k=k, p=p)
+        assert err == 0
+        assert_ids_match(ids, ref, kf, f"{policy} threshold paths k={k} p={p} bf16={bf16}", max_frac=0.25)
