@@ -1237,21 +1237,31 @@ __global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a)
             const unsigned long long Zq = __shfl_sync(FULL, inc, 31);
             const unsigned long long tau = __double2ull_rd(static_cast<double>(frac) * static_cast<double>(Zq));
             const unsigned long long eps = Zq / 1000000ull;
-            // the removed slots are a prefix (cumulative masses only grow):
-            // icut of them; this lane's positions below it weigh nothing
-            unsigned long long cum = inc - sum;
-            bool near = false;
+            // The removed slots are a prefix (cumulative masses only grow):
+            // every slot of the lanes before the first whose inclusive sum
+            // passes tau, and that lane's slots up to tau.  That lane also
+            // holds the cumulative masses on either side of tau (the
+            // boundary check).  icut slots go; the last one always stays.
+            const unsigned over = __ballot_sync(FULL, inc > tau);
+            const int lc = over ? __ffs(over) - 1 : 31;
             int below = 0;
+            bool near = false;
+            if (lane == lc) {
+              unsigned long long cum = inc - sum, lo = cum, hi = ~0ull;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int i = i0 + j;
-              cum += c[j];
-              const bool last = i >= n - 1;
-              below += !last && cum <= tau;
-              if (c[j] && !last && tau < Zq) near |= cum > tau ? (cum - tau < eps) : (tau - cum < eps);
+              for (int j = 0; j < 8; ++j) {
+                cum += c[j];
+                if (cum <= tau) {
+                  ++below;
+                  lo = cum;
+                } else if (hi == ~0ull && i0 + j < n - 1) {
+                  hi = cum;
+                }
+              }
+              near = tau < Zq && (tau - lo < eps || (hi != ~0ull && hi - tau < eps));
             }
-            const int icut = __reduce_add_sync(FULL, static_cast<unsigned>(below));
-            if (__any_sync(FULL, near)) lflags |= Q3S_ROW_TOPP_BOUNDARY;
+            const int icut = min(8 * lc + __shfl_sync(FULL, below, lc), n - 1);
+            if (__shfl_sync(FULL, near, lc)) lflags |= Q3S_ROW_TOPP_BOUNDARY;
             int sa[WCAP / 32];
 #pragma unroll
             for (int r = 0; r < WCAP / 32; ++r) sa[r] = r < P && lane * P + r < n ? asca[lane * P + r] : WCAP;
