@@ -730,8 +730,16 @@ constexpr size_t row_smem_bytes(bool bf16) {
   return sizeof(RowSmem<R, W>) + (bf16 ? 2 * RowSmem<R, W>::VMAX : 0);
 }
 
+// Resident rows per SM each variant is compiled for (its register budget):
+// 64 registers for 16 and 8 warps and for 4-warp bf16 rows, 72 for 4-warp
+// fp32 rows and 2 warps, ~120 for one warp; the widest variants run one row
+// per SM.  Pinned so that code changes do not move the occupancy.
+constexpr int row_min_blocks(int W, bool bf16) {
+  return W >= 12 ? 2 : W == 8 ? 4 : W == 4 ? (bf16 ? 8 : 7) : W == 2 ? 14 : 17;
+}
+
 template <int R, int W, bool BF16>
-__global__ void __launch_bounds__(W * 32) sample_smem_kernel(const SampleArgs a) {
+__global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_kernel(const SampleArgs a) {
   extern __shared__ __align__(16) unsigned char q3s_row_smem[];
   using Smem = RowSmem<R, W>;
   constexpr int RPW = Smem::RPW;
