@@ -131,6 +131,7 @@ struct alignas(16) Scratch {
   uint32_t hist[2][NBINS];
   uint4 cand[CAND];          // {key, index, value/weight bits, spare}
   float noise[CAND];         // Gumbel noise by rank
+  alignas(16) float xs[CAND];  // candidate values by position (exactly-K ranks)
   unsigned long long part_q[2][32];
   float part_f[2][32];
   float part_f2[2][32];
@@ -350,6 +351,104 @@ Q3S_DEV void scan_count_desc(uint32_t* hist, uint32_t krem, uint32_t* sel) {
   }
   hb[0] = make_uint4(0, 0, 0, 0);
   hb[1] = make_uint4(0, 0, 0, 0);
+}
+
+// As scan_count_desc, also recording the count of the next bin down in
+// sel[3] (0 below bin 0); sel[0] = 0xffffffff when fewer than krem entries
+// are counted.
+Q3S_DEV void scan_count_desc_next(uint32_t* hist, uint32_t krem, uint32_t* sel) {
+  const int lane = threadIdx.x;
+  uint4* hb = reinterpret_cast<uint4*>(hist) + 2 * lane;
+  const uint4 a = hb[0], b = hb[1];
+  const uint32_t c[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  const uint32_t below0 = __shfl_up_sync(FULL, c[7], 1);  // bin 8 lane - 1
+  const uint32_t s = (c[0] + c[1]) + (c[2] + c[3]) + (c[4] + c[5]) + (c[6] + c[7]);
+  uint32_t suf = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t n = __shfl_down_sync(FULL, suf, o);
+    if (lane + o < 32) suf += n;
+  }
+  const uint32_t above = suf - s;
+  const bool hit = above < krem && krem <= suf;
+  if (hit) {
+    uint32_t acc = above;
+    bool found = false;
+#pragma unroll
+    for (int i = 7; i >= 0; --i) {
+      if (!found && acc + c[i] >= krem) {
+        found = true;
+        sel[0] = static_cast<uint32_t>(8 * lane + i);
+        sel[1] = c[i];
+        sel[2] = krem - acc;
+        sel[3] = i > 0 ? c[i > 0 ? i - 1 : 0] : (lane > 0 ? below0 : 0u);
+      }
+      acc += c[i];
+    }
+  }
+  if (__ballot_sync(FULL, hit) == 0u && lane == 0) sel[0] = 0xffffffffu;
+  hb[0] = make_uint4(0, 0, 0, 0);
+  hb[1] = make_uint4(0, 0, 0, 0);
+}
+
+// Candidates for the k largest of the values xa (flagged in `mask`) from one
+// histogram of d = max - xa in bins 1/8 wide over d < 32: every entry down to
+// the bin below the one holding the k-th largest.  With every value in
+// [-2000, 2000] an ulp is <= 2^-12, far inside a bin, so values within a few
+// ulps of the ones ranked (approximate keys, temperature-quotient ties) stay
+// in the set.  Returns false, leaving the histogram clear, when that does not
+// apply (NaN, values outside the window, the k-th 32 or more below the top,
+// or more than `stop` candidates); every thread returns the same.
+template <int NT, int E>
+Q3S_DEV bool select_bins8(const float (&xa)[E], uint32_t mask, int k, int stop, Scratch<NT, E>& sh, int& rb,
+                          uint32_t& cmask) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float mx = -INFINITY;
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if ((mask >> j) & 1u) {
+      mx = fmaxf(mx, xa[j]);
+      bad |= xa[j] != xa[j];
+    }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  const bool wbad = __any_sync(FULL, bad);
+  if (lane == 0) {
+    sh.part_f[rb][w] = mx;
+    sh.part_i[rb][w] = wbad;
+  }
+  __syncthreads();
+  float amax = sh.part_f[rb][0];
+  int anyb = sh.part_i[rb][0];
+#pragma unroll
+  for (int i = 1; i < NW; ++i) {
+    amax = fmaxf(amax, sh.part_f[rb][i]);
+    anyb |= sh.part_i[rb][i];
+  }
+  rb ^= 1;
+  if (anyb || !(fabsf(amax) <= 2000.0f)) return false;
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if ((mask >> j) & 1u) {
+      const float e = __fmul_rn(__fsub_rn(amax, xa[j]), 8.0f);
+      if (e < 256.0f) atomicAdd(&sh.hist[0][255u - static_cast<uint32_t>(e)], 1u);
+    }
+  __syncthreads();
+  if (threadIdx.x < 32) scan_count_desc_next(sh.hist[0], static_cast<uint32_t>(k), sh.sel_u);
+  __syncthreads();
+  const uint32_t d = sh.sel_u[0];
+  if (d == 0xffffffffu) return false;
+  const uint32_t b8 = 255u - d;
+  const uint32_t n8 = (static_cast<uint32_t>(k) - sh.sel_u[2]) + sh.sel_u[1] + sh.sel_u[3];
+  if (b8 > 253u || n8 > static_cast<uint32_t>(stop)) return false;
+  const float ecut = static_cast<float>(b8 + 2u);
+  cmask = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if (((mask >> j) & 1u) && __fmul_rn(__fsub_rn(amax, xa[j]), 8.0f) < ecut) cmask |= 1u << j;
+  return true;
 }
 
 // Key of the k-th largest entry (1-based k, multiplicity counted) among the

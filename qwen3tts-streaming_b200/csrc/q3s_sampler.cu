@@ -556,18 +556,25 @@ Q3S_DEV int sample_core(float (&x)[E], uint32_t vmask, uint32_t pmask, float pen
   if (MODE == Q3S_DRAW_GUMBEL && !c.greedy) {
     for (int r = t; r < K; r += NT) sh.noise[r] = __ldg(c.noise + r);
   }
-  uint32_t key[E];
+  float xa[E];
   {
     const float rpen = __frcp_rn(pen);
 #pragma unroll
-    for (int j = 0; j < E; ++j) key[j] = f2key(((dmask >> j) & 1u) ? __fmul_rn(x[j], rpen) : x[j]);
+    for (int j = 0; j < E; ++j) xa[j] = ((dmask >> j) & 1u) ? __fmul_rn(x[j], rpen) : x[j];
   }
-  const uint32_t thr = select_threshold<NT, E>(key, vmask, K, FINISH + K / 2, sh, rb);
-  const uint32_t lo = thr > 40u ? thr - 40u : 0u;
+  // candidates: one 1/8-unit histogram below the largest value where that
+  // locates the K-th tightly, else a radix threshold with a 40-ulp margin
   uint32_t cmask = 0;
+  if (!select_bins8<NT, E>(xa, vmask, K, FINISH + K, sh, rb, cmask)) {
+    uint32_t key[E];
 #pragma unroll
-  for (int j = 0; j < E; ++j)
-    if (((vmask >> j) & 1u) && key[j] >= lo) cmask |= 1u << j;
+    for (int j = 0; j < E; ++j) key[j] = f2key(xa[j]);
+    const uint32_t thr = select_threshold<NT, E>(key, vmask, K, FINISH + K / 2, sh, rb);
+    const uint32_t lo = thr > 40u ? thr - 40u : 0u;
+#pragma unroll
+    for (int j = 0; j < E; ++j)
+      if (((vmask >> j) & 1u) && key[j] >= lo) cmask |= 1u << j;
+  }
   uint32_t n;
   const uint32_t pos0 = block_excl_scan_u<NT, E>(__popc(cmask), n, sh, rb);
   if (n > static_cast<uint32_t>(CAND)) {
@@ -579,6 +586,7 @@ Q3S_DEV int sample_core(float (&x)[E], uint32_t vmask, uint32_t pmask, float pen
   }
   // candidate records in vocabulary order: {s or x' bits, index, x' bits, weight bits}
   const int n4 = (static_cast<int>(n) + 3) & ~3;
+  bool nonfinite = false;
   {
     uint32_t pos = pos0;
 #pragma unroll
@@ -586,29 +594,51 @@ Q3S_DEV int sample_core(float (&x)[E], uint32_t vmask, uint32_t pmask, float pen
       if ((cmask >> j) & 1u) {
         const float xe = ((dmask >> j) & 1u) ? __fdiv_rn(x[j], pen) : x[j];
         sh.cand[pos] = make_uint4(0u, static_cast<uint32_t>(v0 + j), __float_as_uint(xe), 0u);
+        sh.xs[pos] = xe;
+        nonfinite |= !isfinite(xe);
         ++pos;
       }
-    for (int i = static_cast<int>(n) + t; i < n4; i += NT)
+    for (int i = static_cast<int>(n) + t; i < n4; i += NT) {
       sh.cand[i] = make_uint4(0xff800000u, 0x7fffffffu, 0xff800000u, 0u);  // -inf, never outranks
+      sh.xs[i] = -INFINITY;
+    }
   }
-  __syncthreads();
+  nonfinite = __syncthreads_or(nonfinite) != 0;
 
   if (MODE == Q3S_DRAW_GUMBEL || c.greedy) {
     // exactly-K by (x' desc, index asc) (talker_unified_modules.py:415,
-    // utils.py:1189); score x'/T + noise[rank]; argmax, lowest rank on ties
+    // utils.py:1189); score x'/T + noise[rank]; argmax, lowest rank on ties.
+    // Positions are in vocabulary order, so the rank of position i counts
+    // x >= x_i before it and x > x_i after it: with every x' finite, one
+    // compare per entry -- x > (the float below x_i) in quads wholly before
+    // i's, x > x_i elsewhere, then the equal entries earlier in i's quad.
     float bs = -INFINITY;
     int br = 0x7fffffff, bid = 0x7fffffff;
+    const float4* xs4 = reinterpret_cast<const float4*>(sh.xs);
     for (int i = t; i < static_cast<int>(n); i += NT) {
       const uint4 me = sh.cand[i];
       const float xi = __uint_as_float(me.z);
       const int ii = static_cast<int>(me.y);
       int rank = 0;
-      for (int o = 0; o < n4; o += 4) {
+      if (!nonfinite) {
+        const uint32_t bi = __float_as_uint(xi);
+        const float xd = xi > 0.0f ? __uint_as_float(bi - 1u) : (xi < 0.0f ? __uint_as_float(bi + 1u) : -0x1p-149f);
+        const int p4 = i >> 2;
+#pragma unroll 4
+        for (int q4 = 0; q4 < (n4 >> 2); ++q4) {
+          const float4 f = xs4[q4];
+          const float th = q4 < p4 ? xd : xi;
+          rank += (f.x > th) + (f.y > th) + (f.z > th) + (f.w > th);
+        }
+        for (int q = 4 * p4; q < i; ++q) rank += sh.xs[q] == xi;
+      } else {
+        for (int o = 0; o < n4; o += 4) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint4 ot = sh.cand[o + u];
-          const float xo = __uint_as_float(ot.z);
-          rank += (xo > xi) | ((xo == xi) & (static_cast<int>(ot.y) < ii));
+          for (int u = 0; u < 4; ++u) {
+            const uint4 ot = sh.cand[o + u];
+            const float xo = __uint_as_float(ot.z);
+            rank += (xo > xi) | ((xo == xi) & (static_cast<int>(ot.y) < ii));
+          }
         }
       }
       if (rank < K) {
