@@ -1013,11 +1013,15 @@ __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
           // flight so none lands after exit, then leave
           if (t == 0) {
             if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
-            for (int h = g; h < min(g + a.nbuf, nitems); ++h)
+            const int issued = g == 0 ? a.nbuf : a.nbuf - 1;  // items g .. g + issued - 1
+            for (int h = g; h < min(g + issued, nitems); ++h)
               (void)mbar_wait_bounded(&bars[h % a.nbuf], static_cast<uint32_t>((h / a.nbuf) & 1));
           }
           return;
         }
+        // every thread has passed this barrier after reading the previous
+        // stage's slot: it takes the item nbuf - 1 stages ahead
+        if (t == 0 && g > 0 && g - 1 + a.nbuf < nitems) issue(g - 1 + a.nbuf);
         const unsigned char* row = ring + static_cast<size_t>(slot) * a.row_bytes;
 #pragma unroll
         for (int e = 0; e < E; ++e) {
@@ -1031,8 +1035,6 @@ __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
             vmask |= 1u << e;
           }
         }
-        __syncthreads();  // every thread has read the slot
-        if (t == 0 && g + a.nbuf < nitems) issue(g + a.nbuf);
       } else {
         // every thread is done with the previous stage's shared state
         __syncthreads();

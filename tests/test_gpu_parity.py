@@ -523,3 +523,40 @@ def test_warp_kernel_threshold_paths(cuda_device, q3s_lib, policy, bf16):
         ids, kf, err, ref = _warp_case(cuda_device, x, bf16=bf16, policy=policy, T=T, k=k, p=p)
         assert err == 0
         assert_ids_match(ids, ref, kf, f"{policy} threshold paths k={k} p={p} bf16={bf16}", max_frac=0.25)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_gumbel_candidate_paths(cuda_device, q3s_lib, bf16):
+    """Exactly-K Gumbel rows through each way the CTA sampler finds its
+    candidates (1/8-unit bins below the row maximum, the radix threshold for
+    values beyond +-2000, NaN-free rows too dense or too peaked for the bins),
+    with ties across the K boundary (lowest index first), -inf and suppressed
+    entries, and a repetition penalty over a packed history."""
+    rng = np.random.default_rng(31)
+    B, V = 12, 3072
+    x = (rng.standard_normal((B, V)) * 3).astype(np.float32)
+    x[1, :120] = 4.0                                   # 120-way tie across K = 50
+    x[2] = rng.standard_normal(V) * 0.01               # dense: radix threshold
+    x[3] = rng.standard_normal(V); x[3, 9] = 60.0      # K-th far below the top
+    x[4] = rng.standard_normal(V) * 1000.0             # beyond +-2000
+    x[5, ::2] = -np.inf                                # half the row -inf
+    x[6, 7] = 1e30                                     # one dominant entry
+    x[7] = np.round(rng.standard_normal(V) * 8) / 8    # many exact ties
+    x[8, :3000] = -1e9                                 # suppressed block: fewer than K above it
+    xt = torch.from_numpy(x)
+    if bf16:
+        xt = xt.to(torch.bfloat16)
+        x = xt.float().numpy()
+    noise = (-np.log(-np.log(rng.random((B, 50)).clip(1e-12, 1 - 1e-7)))).astype(np.float32)
+    T = np.full(B, 0.9, np.float32)
+    pen = np.full(B, 1.15, np.float32)
+    hist = [rng.integers(0, V, int(n)).astype(np.int32) for n in rng.integers(0, 600, B)]
+    offs = np.zeros(B + 1, np.int32)
+    offs[1:] = np.cumsum([len(h) for h in hist])
+    flat = np.concatenate(hist).astype(np.int32)
+    ids = q3s.sample_packed(xt.to(cuda_device), _dev(flat, cuda_device), _dev(offs, cuda_device), mode="gumbel",
+                            topk=50, gumbel_noise=_dev(noise, cuda_device), temperature=_dev(T, cuda_device),
+                            penalty=_dev(pen, cuda_device), eos_id=-1)
+    ref = O.sample_gumbel(x, gumbel_noise=noise, temperature=T, penalty=pen, history=flat, offsets=offs,
+                          topk=50, eos_id=-1)
+    np.testing.assert_array_equal(ids.cpu().numpy(), ref["ids"])
