@@ -186,6 +186,22 @@ int32_t q3s_abi_version(void);
  * can check its own struct layout (which: 0 = sample, 1 = cp_frame). */
 uint32_t q3s_desc_size(int32_t which);
 
+/* Per-row randomness on the device (the next step after the sampler: the
+ * reference draws it per slot on the host side of the launch,
+ * engine/backend/executor.py:3216-3295 -- one torch.rand per slot and step,
+ * then -log(-log(clamp(u, 1e-8, 1))) for the Gumbel noise).  One launch fills
+ * out[i, 0..cols) for rows i = 0..rows-1 from Philox4x32-10 keyed by `seed`:
+ * block j of row key r (row_keys[i], or row0 + i when row_keys is NULL) at
+ * `step` uses counter (j, r mod 2^32, step, 0xA5A5); a 32-bit output x
+ * becomes the uniform (x >> 8) * 2^-24 in [0, 1).  The same bits as the host
+ * generator q3s/philox.py (row_uniforms), so a row's numbers do not depend on
+ * which batch or shard it sits in.  `out` and `row_keys` are device
+ * pointers; asynchronous on `stream`. */
+#define Q3S_PHILOX_UNIFORM 0   /* uniforms in [0, 1) (one per row for the icdf draw) */
+#define Q3S_PHILOX_GUMBEL 1    /* -log(-log(max(u, 1e-8))) in fp32 (gumbel_noise) */
+q3s_status q3s_philox_rows(uint64_t seed, uint32_t step, const int64_t* row_keys, int64_t row0, int32_t rows,
+                           int32_t cols, int32_t kind, float* out, int64_t out_row_stride, void* stream);
+
 /* Kernel family for icdf steps that either family can serve (process-wide;
  * a tuning and test knob with no counterpart in the reference interface):
  * the register-resident CTA-per-row kernel, or the shared-memory-resident

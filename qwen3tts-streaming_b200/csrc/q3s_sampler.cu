@@ -27,6 +27,7 @@
 
 #include "q3s_args.cuh"
 #include "q3s_device.cuh"
+#include "q3s_philox.cuh"
 #include "q3s_sampler.h"
 
 namespace q3s {
@@ -1177,6 +1178,28 @@ int32_t q3s_abi_version(void) { return Q3S_ABI_VERSION; }
 int32_t q3s_set_kernel_policy(int32_t policy) {
   if (policy < Q3S_POLICY_AUTO || policy > Q3S_POLICY_ROW_WMAX) return -1;
   return __atomic_exchange_n(&g_policy, policy, __ATOMIC_RELAXED);
+}
+
+q3s_status q3s_philox_rows(uint64_t seed, uint32_t step, const int64_t* row_keys, int64_t row0, int32_t rows,
+                           int32_t cols, int32_t kind, float* out, int64_t out_row_stride, void* stream) {
+  if (rows < 0 || cols < 0) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_rows: rows=%d cols=%d", rows, cols);
+  if (kind != Q3S_PHILOX_UNIFORM && kind != Q3S_PHILOX_GUMBEL)
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_rows: unknown kind %d", kind);
+  if (rows == 0 || cols == 0) return ok();
+  if (!out) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_rows: out is NULL");
+  if (out_row_stride < cols)
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_rows: out_row_stride %lld < cols %d",
+                static_cast<long long>(out_row_stride), cols);
+  const int64_t threads = static_cast<int64_t>(rows) * ((cols + 3) / 4);
+  const int nt = 256;
+  const int64_t grid = (threads + nt - 1) / nt;
+  if (grid > 0x7fffffffLL) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_rows: too many rows x columns");
+  q3s::philox_rows_kernel<<<static_cast<unsigned>(grid), nt, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32), step, row_keys, row0, rows, cols, kind, out,
+      out_row_stride);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_philox_rows launch failed: %s", cudaGetErrorString(e));
+  return ok();
 }
 
 uint32_t q3s_desc_size(int32_t which) {

@@ -9,6 +9,7 @@ from .ops import (
     CpFramePlan,
     SamplePlan,
     kernel_policy,
+    philox_rows,
     sample_codebook0,
     sample_cp_frame,
     sample_packed,
@@ -23,6 +24,7 @@ __all__ = [
     "CpFramePlan",
     "SamplePlan",
     "kernel_policy",
+    "philox_rows",
     "sample_codebook0",
     "sample_cp_frame",
     "sample_packed",

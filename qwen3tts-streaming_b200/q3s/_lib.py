@@ -24,6 +24,7 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 CP_DIRECT, CP_ROTATE = 0, 1
 POLICY_AUTO, POLICY_CTA, POLICY_WARP = 0, 1, 2
 POLICY_ROW_W = {1: 3, 2: 4, 4: 5, 8: 6, "max": 7}
+PHILOX_UNIFORM, PHILOX_GUMBEL = 0, 1
 
 ROW_DRAW_BOUNDARY, ROW_TOPP_BOUNDARY, ROW_GREEDY, ROW_FALLBACK = 1, 2, 4, 8
 DEVERR_HISTORY_ID, DEVERR_OFFSETS, DEVERR_NO_MASS, DEVERR_WAIT_TIMEOUT, DEVERR_CANDIDATES = 1, 2, 4, 8, 16
@@ -110,6 +111,7 @@ EXPORTS = (
     "q3s_abi_version",
     "q3s_desc_size",
     "q3s_set_kernel_policy",
+    "q3s_philox_rows",
 )
 
 _lock = threading.Lock()
@@ -140,6 +142,9 @@ def load(path: str | Path | None = None) -> C.CDLL:
         lib.q3s_desc_size.restype = C.c_uint32
         lib.q3s_set_kernel_policy.argtypes = [C.c_int32]
         lib.q3s_set_kernel_policy.restype = C.c_int32
+        lib.q3s_philox_rows.argtypes = [C.c_uint64, C.c_uint32, _p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
+                                        _p, C.c_int64, _p]
+        lib.q3s_philox_rows.restype = C.c_int
         if lib.q3s_abi_version() != Q3S_ABI_VERSION:
             raise RuntimeError(f"q3s ABI {lib.q3s_abi_version()} != binding {Q3S_ABI_VERSION}; rebuild")
         for which, st in ((0, SampleDesc), (1, CpFrameDesc)):

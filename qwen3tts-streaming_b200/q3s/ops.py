@@ -112,6 +112,42 @@ def _stream_handle(stream: Optional[torch.cuda.Stream]) -> int:
 # plans: a filled descriptor plus the tensors it points at
 # ---------------------------------------------------------------------------
 
+def philox_rows(seed: int, rows: int, cols: int, *, step: int = 0, row0: int = 0,
+                row_keys: Optional[torch.Tensor] = None, kind: str = "uniform",
+                device: Optional[torch.device] = None, out: Optional[torch.Tensor] = None,
+                stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Per-row randomness generated on the GPU in one launch: fp32 ``[rows, cols]``
+    uniforms in [0, 1) (``kind="uniform"``) or Gumbel noise
+    ``-log(-log(max(u, 1e-8)))`` (``kind="gumbel"``), the same bits as
+    ``q3s.philox.row_uniforms(seed, keys, cols, step)`` for the row keys
+    ``row_keys`` (int64, on the device) or ``row0 .. row0+rows-1``.  Replaces
+    the reference's per-slot ``torch.rand`` + noise transform
+    (engine/backend/executor.py:3216-3295)."""
+    lib = _lib.load()
+    if kind not in ("uniform", "gumbel"):
+        raise ValueError(f"kind must be 'uniform' or 'gumbel', got {kind!r}")
+    if row_keys is not None:
+        dev = row_keys.device
+        if dev.type != "cuda":
+            raise RuntimeError("row_keys must be a CUDA tensor (no CPU fallback)")
+        row_keys = row_keys.reshape(-1).to(torch.int64).contiguous()
+        if row_keys.numel() != rows:
+            raise ValueError(f"row_keys has {row_keys.numel()} entries for {rows} rows")
+    else:
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty(rows, cols, dtype=torch.float32, device=dev)
+    elif out.dtype != torch.float32 or out.dim() != 2 or out.shape != (rows, cols) or out.stride(1) != 1:
+        raise ValueError("out must be fp32 [rows, cols] with unit column stride")
+    kcode = _lib.PHILOX_UNIFORM if kind == "uniform" else _lib.PHILOX_GUMBEL
+    _lib.check(lib.q3s_philox_rows(int(seed) & 0xFFFFFFFFFFFFFFFF, int(step) & 0xFFFFFFFF,
+                                   row_keys.data_ptr() if row_keys is not None else None, int(row0), int(rows),
+                                   int(cols), kcode, out.data_ptr() if out.numel() else None,
+                                   out.stride(0) if out.numel() else cols, _stream_handle(stream)),
+               "q3s_philox_rows")
+    return out
+
+
 def set_kernel_policy(policy: str) -> str:
     """Choose the kernel family for icdf steps (process-wide): "auto", "cta"
     (register-resident CTA per row), "warp" (shared-memory row kernel, warps

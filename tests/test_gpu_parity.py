@@ -560,3 +560,28 @@ def test_gumbel_candidate_paths(cuda_device, q3s_lib, bf16):
     ref = O.sample_gumbel(x, gumbel_noise=noise, temperature=T, penalty=pen, history=flat, offsets=offs,
                           topk=50, eos_id=-1)
     np.testing.assert_array_equal(ids.cpu().numpy(), ref["ids"])
+
+
+def test_philox_rows_match_host_generator(cuda_device, q3s_lib):
+    """Device-side per-row uniforms are bit-identical to the host generator
+    (q3s/philox.py row_uniforms) for contiguous and arbitrary row keys, steps
+    and column counts; the Gumbel transform agrees with the torch fp32
+    transform of the same uniforms within 1e-6 (relative and absolute: both
+    use a correctly-rounded-within-1-ulp log)."""
+    from q3s import philox as P
+    rng = np.random.default_rng(41)
+    cases = [(0, 0, 1, 1, 0), (2**40 + 12345, 7, 128, 50, 0), (2**64 - 1, 3, 1000, 3, 5000),
+             (987654321, 0, 128, 750, 0), (5, 2**32 - 1, 33, 4, 2**33 + 17)]
+    for seed, step, rows, cols, row0 in cases:
+        keys = np.arange(row0, row0 + rows, dtype=np.int64)
+        want = P.row_uniforms(seed, keys, cols=cols, step=step)
+        got = q3s.philox_rows(seed, rows, cols, step=step, row0=row0, device=cuda_device).cpu().numpy()
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+        g = q3s.philox_rows(seed, rows, cols, step=step, row0=row0, kind="gumbel", device=cuda_device).cpu().numpy()
+        np.testing.assert_allclose(g, P.gumbel_from_uniforms(want), rtol=1e-6, atol=1e-6)
+    # arbitrary slot keys (engine slots), including keys past 2^32
+    keys = rng.integers(0, 2**40, 257).astype(np.int64)
+    want = P.row_uniforms(77, keys, cols=15 * 50, step=9)
+    got = q3s.philox_rows(77, 257, 15 * 50, step=9, row_keys=_dev(keys, cuda_device)).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert float(got.min()) >= 0.0 and float(got.max()) < 1.0
