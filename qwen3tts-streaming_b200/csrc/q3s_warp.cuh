@@ -20,6 +20,8 @@
 // kept) -> top-p (stable ascending order) -> softmax -> inverse CDF.
 #pragma once
 
+#include <type_traits>
+
 #include "q3s_args.cuh"
 #include "q3s_device.cuh"
 
@@ -916,8 +918,10 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
   //      gate (-inf), the repetition penalty.  Candidate rows defer the
   //      division of present entries > 0 (x * RN(1/pen) keys select first);
   //      whole-vocabulary rows compute s = x'/T here.  Branch-free per entry:
-  //      the selects replace data-dependent branches ------------------------
-  {
+  //      the selects replace data-dependent branches; the row's path picks
+  //      one of two loops, so neither carries the other's arithmetic -------
+  auto first_pass = [&](auto cand_tag) {
+    constexpr bool IS_CAND = decltype(cand_tag)::value;
     const uint2* stg = reinterpret_cast<const uint2*>(stage);  // bf16 quad h at stg[h]
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
@@ -948,7 +952,7 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
           app |= (sup ? 16u : 0u) << j;
           float x = sup ? NEG_SUPPRESS : v[j];
           x = (gate && 4 * h + j == eos_id) ? -INFINITY : x;
-          if (cand_path) {
+          if constexpr (IS_CAND) {
             // the approximate value: x * pen for present entries <= 0 (exact),
             // x * RN(1/pen) for present entries > 0 (within 2 ulps of x / pen)
             x = ap ? __fmul_rn(x, x > 0.0f ? rpen : pen) : x;
@@ -970,7 +974,11 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
         sh.appb[h] = static_cast<uint8_t>(app);
       }
     }
-  }
+  };
+  if (cand_path)
+    first_pass(std::true_type{});
+  else
+    first_pass(std::false_type{});
   row_sync<W>();  // the row is processed; the presence flags are dead
 
   bool done = false;
