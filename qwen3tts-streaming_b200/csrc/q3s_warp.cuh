@@ -1078,30 +1078,38 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
       });
       lo = thr > 40u ? thr - 40u : 0u;
     }
-    // candidates: masks per quad, then records in vocabulary order
+    // candidates: masks per quad (one loop per selection kind, picked once
+    // per row), then records in vocabulary order
     uint32_t cnt = 0;
+    auto mask_pass = [&](auto linear_tag) {
+      constexpr bool LIN = decltype(linear_tag)::value;
 #pragma unroll 2
-    for (int r = rb0; r < rb1; ++r) {
-      const int h = lane + 32 * r;
-      uint32_t cm = 0;
-      if (4 * h < V) {
-        const float4 q = sh.row[h];
-        const float v[4] = {q.x, q.y, q.z, q.w};
+      for (int r = rb0; r < rb1; ++r) {
+        const int h = lane + 32 * r;
+        uint32_t cm = 0;
+        if (4 * h < V) {
+          const float4 q = sh.row[h];
+          const float v[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          bool c;
-          if (linear) {
-            const float d = dist(v[j]);
-            c = d < dcut || __fmul_rn(__fsub_rn(d, dcut), dsc) < ecut;
-          } else {
-            c = f2key(v[j]) >= lo;
+          for (int j = 0; j < 4; ++j) {
+            bool c;
+            if constexpr (LIN) {
+              const float d = dist(v[j]);
+              c = d < dcut || __fmul_rn(__fsub_rn(d, dcut), dsc) < ecut;
+            } else {
+              c = f2key(v[j]) >= lo;
+            }
+            cm |= (c ? 1u : 0u) << j;
           }
-          cm |= (c ? 1u : 0u) << j;
         }
+        sh.cmask[h] = static_cast<uint8_t>(cm);
+        cnt += __popc(cm);
       }
-      sh.cmask[h] = static_cast<uint8_t>(cm);
-      cnt += __popc(cm);
-    }
+    };
+    if (linear)
+      mask_pass(std::true_type{});
+    else
+      mask_pass(std::false_type{});
 #pragma unroll
     for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
     uint32_t n32;
@@ -1358,27 +1366,38 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
         //      bits (monotone in s) ------------------------------------------
         const bool cut = top_p < 1.0f;
         constexpr uint32_t LO = (1u << MASS_LO_BITS) - 1u;
+        // one loop per (top-k, top-p) combination, picked once per row
+        auto weights_pass = [&](auto topk_tag, auto cut_tag) {
+          constexpr bool TOPK = decltype(topk_tag)::value, CUT = decltype(cut_tag)::value;
 #pragma unroll 2
-        for (int r = rb0; r < rb1; ++r) {
-          const int h = lane + 32 * r;
-          if (4 * h >= V) continue;
-          const float4 f = sh.row[h];
-          const float sv[4] = {f.x, f.y, f.z, f.w};
-          float wv[4];
+          for (int r = rb0; r < rb1; ++r) {
+            const int h = lane + 32 * r;
+            if (4 * h >= V) continue;
+            const float4 f = sh.row[h];
+            const float sv[4] = {f.x, f.y, f.z, f.w};
+            float wv[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const bool surv = !topk || f2key(sv[j]) >= kth;
-            wv[j] = surv ? softmax_weight(sv[j], m) : 0.0f;
-            if (cut) {
-              const unsigned long long q = mass_fixed(wv[j]);
-              if (q) {
-                const uint32_t bn = coarse_bin(wv[j]);
-                atomicAdd(&sh.hist[0][bn], static_cast<uint32_t>(q >> MASS_LO_BITS));
-                atomicAdd(&sh.hist[1][bn], static_cast<uint32_t>(q) & LO);
+            for (int j = 0; j < 4; ++j) {
+              const bool surv = !TOPK || f2key(sv[j]) >= kth;
+              wv[j] = surv ? softmax_weight(sv[j], m) : 0.0f;
+              if constexpr (CUT) {
+                const unsigned long long q = mass_fixed(wv[j]);
+                if (q) {
+                  const uint32_t bn = coarse_bin(wv[j]);
+                  atomicAdd(&sh.hist[0][bn], static_cast<uint32_t>(q >> MASS_LO_BITS));
+                  atomicAdd(&sh.hist[1][bn], static_cast<uint32_t>(q) & LO);
+                }
               }
             }
+            sh.row[h] = make_float4(wv[0], wv[1], wv[2], wv[3]);
           }
-          sh.row[h] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+        };
+        if (topk) {
+          if (cut) weights_pass(std::true_type{}, std::true_type{});
+          else weights_pass(std::true_type{}, std::false_type{});
+        } else {
+          if (cut) weights_pass(std::false_type{}, std::true_type{});
+          else weights_pass(std::false_type{}, std::false_type{});
         }
         row_sync<W>();
         bool single = false;
