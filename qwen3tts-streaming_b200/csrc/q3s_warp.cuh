@@ -920,8 +920,9 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
   //      whole-vocabulary rows compute s = x'/T here.  Branch-free per entry:
   //      the selects replace data-dependent branches; the row's path picks
   //      one of two loops, so neither carries the other's arithmetic -------
-  auto first_pass = [&](auto cand_tag) {
+  auto first_pass = [&](auto cand_tag, auto divt_tag, auto greedy_tag) {
     constexpr bool IS_CAND = decltype(cand_tag)::value;
+    constexpr bool DIVT = decltype(divt_tag)::value, GREEDY = decltype(greedy_tag)::value;
     const uint2* stg = reinterpret_cast<const uint2*>(stage);  // bf16 quad h at stg[h]
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
@@ -961,9 +962,9 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
           } else {
             const float dv = __fdiv_rn(x, pen), mv = __fmul_rn(x, pen);
             x = ap ? (x > 0.0f ? dv : mv) : x;
-            if (divT) x = __fdiv_rn(x, T);
+            if constexpr (DIVT) x = __fdiv_rn(x, T);
             lm = fmaxf(lm, x);
-            if (greedy && arg_better(x, 4 * h + j, gv, gi)) {
+            if (GREEDY && arg_better(x, 4 * h + j, gv, gi)) {
               gv = x;
               gi = 4 * h + j;
             }
@@ -976,9 +977,13 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
     }
   };
   if (cand_path)
-    first_pass(std::true_type{});
+    first_pass(std::true_type{}, std::false_type{}, std::false_type{});
+  else if (greedy)
+    first_pass(std::false_type{}, std::false_type{}, std::true_type{});
+  else if (divT)
+    first_pass(std::false_type{}, std::true_type{}, std::false_type{});
   else
-    first_pass(std::false_type{});
+    first_pass(std::false_type{}, std::false_type{}, std::false_type{});
   row_sync<W>();  // the row is processed; the presence flags are dead
 
   bool done = false;
