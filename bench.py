@@ -31,6 +31,7 @@ import statistics
 import subprocess
 import sys
 import threading
+import types
 import time
 from pathlib import Path
 
@@ -54,6 +55,8 @@ def parse_args():
     ap.add_argument("--profile-config", type=int, default=None,
                     help="plain eager launches of one config (0-4; 2 = code-predictor frame) for ncu; "
                          "prints no bench value")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="with --profile-config 1 or 4: the launches are q3s_step_update over that config's history")
     return ap.parse_args()
 
 
@@ -271,6 +274,49 @@ def measure_config(cfg, rows, total_rows, world, dev, stream, steps, warmup):
     return max_ranks(ms, world, dev), bytes_step, b.B
 
 
+class _StepPlan:
+    """One q3s_step_update launch over its own history copy (the launch
+    writes history_out / offsets_out; the guard state is shared)."""
+
+    def __init__(self, guard, ids, history, offsets):
+        import torch
+
+        self.guard, self.ids, self.history, self.offsets = guard, ids, history, offsets
+        self.h_out = torch.empty(history.numel() + ids.numel(), dtype=torch.int32, device=history.device)
+        self.o_out = torch.empty(offsets.numel(), dtype=torch.int32, device=history.device)
+
+    def launch(self, stream):
+        self.guard.step(self.ids, history=self.history, offsets=self.offsets, history_out=self.h_out,
+                        offsets_out=self.o_out, stream=stream)
+
+
+def measure_step(cfg, rows, total_rows, world, dev, stream, steps, warmup):
+    """Graph-timed q3s_step_update (EOS + loop guard + packed history append)
+    on the history of one codebook-0 config; returns (ms/step, bytes/step, B)."""
+    import numpy as np
+    import torch
+
+    import q3s
+    from q3s import step as qstep
+    from q3s import workloads
+
+    b = workloads.make_batch(cfg, rows=rows, total_rows=total_rows).to(dev)
+    B, L = b.B, b.history.numel()
+    rng = np.random.default_rng(4242 + cfg)
+    guard = q3s.StepGuard(B, device=dev)  # reference SchedulerConfig thresholds (4 / 10 / 2.0 / 20)
+    guard.set_progress(frame_idx=rng.integers(0, 200, B), decode_start_frame=rng.integers(0, 50, B),
+                       text_tokens_consumed=rng.integers(0, 100, B), input_complete=rng.random(B) < 0.7)
+    ids = torch.from_numpy(rng.integers(0, 2048, B)).to(dev)
+    bytes_step = qstep.algorithmic_bytes(B, L)
+    plans = [_StepPlan(guard, ids, b.history, b.offsets)]
+    plans += [_StepPlan(guard, ids, b.history.clone(), b.offsets.clone()) for _ in range(n_copies(bytes_step) - 1)]
+    gt = GraphTimer(plans, stream)
+    gt.run(warmup)
+    ms = timed(world, stream, lambda: gt.run(steps)) / steps
+    gt.release()
+    return max_ranks(ms, world, dev), bytes_step, B
+
+
 def measure_cp(rows, total_rows, world, dev, stream, frames, warmup):
     """Code-predictor frame: persistent kernel vs 15 single-stage launches."""
     import torch
@@ -472,6 +518,14 @@ def run_q3s(args):
                                        "tokens_per_s": round(n / (ms / 1000)), "rows_per_gpu": bb,
                                        "achieved_gbs_per_gpu": round(gbs, 1),
                                        "frac_of_measured_hbm": round(gbs / peaks()[0], 4)}
+        for cfg, n, steps in ((1, 128 * world, 2000), (4, 4096, 400)):
+            rr = shard.row_range(rank, world, n)
+            ms, by, bb = measure_step(cfg, rr, n, world, dev, stream, steps, 20)
+            gbs = by / (ms / 1000) / 1e9
+            extra[f"step_update_cfg{cfg}_B{n}"] = {"us_per_step": round(1000 * ms, 3), "rows_per_gpu": bb,
+                                                   "achieved_gbs_per_gpu": round(gbs, 1),
+                                                   "frac_of_measured_hbm": round(gbs / peaks()[0], 4),
+                                                   "d2h_bytes_per_step": 4}
         rr = shard.row_range(rank, world, 128 * world)
         msp, ms15, cpb, cb = measure_cp(rr, 128 * world, world, dev, stream, 1000, 20)
         extra["cfg2_cp_frame_B128"] = {"persistent_us_per_frame": round(1000 * msp, 3),
@@ -589,7 +643,17 @@ def run_profile(args):
     torch.cuda.set_device(dev)
     q3s.load_library()
     cfg = args.profile_config
-    if cfg == 2:
+    if args.profile_step:
+        import numpy as np
+
+        b = workloads.make_batch(cfg).to(dev)
+        rng = np.random.default_rng(4242 + cfg)
+        guard = q3s.StepGuard(b.B, device=dev)
+        ids = torch.from_numpy(rng.integers(0, 2048, b.B)).to(dev)
+        plans = [_StepPlan(guard, ids, b.history if i == 0 else b.history.clone(), b.offsets) for i in range(4)]
+        stream = torch.cuda.current_stream()
+        plans = [types.SimpleNamespace(launch=lambda p=p: p.launch(stream)) for p in plans]
+    elif cfg == 2:
         f = workloads.make_cp_frame().to(dev)
         plans = [q3s.CpFramePlan(f.base if i == 0 else f.base.clone(), mode="gumbel", topk=50,
                                  ids_init=f.ids_init, rotate=True, temperature=f.temperature,
@@ -601,7 +665,8 @@ def run_profile(args):
     for i in range(n):
         plans[i % len(plans)].launch()
     torch.cuda.synchronize()
-    print(json.dumps({"profile": True, "config": cfg, "launches": n}), flush=True)
+    print(json.dumps({"profile": True, "config": cfg, "step_update": bool(args.profile_step), "launches": n}),
+          flush=True)
 
 
 def main():

@@ -182,8 +182,8 @@ const char* q3s_last_error_string(void);
 /* Q3S_ABI_VERSION of the loaded library. */
 int32_t q3s_abi_version(void);
 
-/* sizeof() of the two descriptors as compiled into the library, so a binding
- * can check its own struct layout (which: 0 = sample, 1 = cp_frame). */
+/* sizeof() of the descriptors as compiled into the library, so a binding can
+ * check its own struct layout (which: 0 = sample, 1 = cp_frame, 2 = step). */
 uint32_t q3s_desc_size(int32_t which);
 
 /* Per-row randomness on the device (the next step after the sampler: the
@@ -201,6 +201,72 @@ uint32_t q3s_desc_size(int32_t which);
 #define Q3S_PHILOX_GUMBEL 1    /* -log(-log(max(u, 1e-8))) in fp32 (gumbel_noise) */
 q3s_status q3s_philox_rows(uint64_t seed, uint32_t step, const int64_t* row_keys, int64_t row0, int32_t rows,
                            int32_t cols, int32_t kind, float* out, int64_t out_row_stride, void* stream);
+
+/* Per-step codec-0 epilogue on the device: EOS, frame counter, token loop
+ * guard, packed history append.  The reference reads every row's codebook-0
+ * id back to the host each step (engine/backend/executor.py:532-546) and runs
+ * these checks per slot in Python (engine/backend/engine_loop.py:2749-2750,
+ * 2863-3080, thresholds normalised at :372-387); the count update it feeds is
+ * talker_unified_modules.py:421-422.  One launch does them for all rows and
+ * leaves a compact event list, so the host reads one word per step (the event
+ * count) and the listed rows only when it is non-zero. */
+#define Q3S_EVT_EOS 1              /* id == eos_id: segment ends, guard skipped */
+#define Q3S_EVT_SUSPECT 2          /* loop_run reached the suspect threshold */
+#define Q3S_EVT_RECOVERED 4        /* token changed after a run >= suspect */
+#define Q3S_EVT_DEFERRED 8         /* run == abort without generation progress */
+#define Q3S_EVT_ABORT_PROGRESS 16  /* run >= abort with progress ("progress" mode) */
+#define Q3S_EVT_ABORT_EMERGENCY 32 /* run >= emergency ("emergency" mode) */
+
+typedef struct q3s_step_desc {
+  uint32_t struct_size;        /* = sizeof(q3s_step_desc) */
+  int32_t batch;               /* B >= 0 (0 = no-op), < 2^23 */
+  const int64_t* ids_i64;      /* [B] sampled codebook-0 ids: exactly one of the two */
+  const int32_t* ids_i32;
+  int32_t eos_id;              /* codec EOS id (reference: 2150) */
+  int32_t reserved0;
+
+  /* packed history append (history_out NULL = skipped).  Row b of the output
+   * is row b of the input followed by ids[b]; offsets_out[b] = offsets[b] + b.
+   * history_out must not overlap history. */
+  const int32_t* history;      /* packed ids; row b = history[offsets[b] .. offsets[b+1]) */
+  const int32_t* offsets;      /* [B+1] */
+  int64_t history_len;         /* entries in `history` (bounds check) */
+  int32_t* history_out;        /* capacity history_out_capacity entries (>= history_len + B) */
+  int32_t* offsets_out;        /* [B+1] */
+  int64_t history_out_capacity;
+
+  /* loop guard thresholds as given to the engine (normalised inside as the
+   * engine does: abort <= 0 turns the guard off) */
+  int32_t suspect_frames;
+  int32_t abort_frames;
+  int32_t emergency_frames;
+  int32_t reserved1;
+  double min_audio_text_ratio; /* <= 0: no progress gate */
+
+  /* per-row guard state [B], read and updated in place (the engine keeps it
+   * per segment / slot; a new or retried segment starts at loop_token = -1 and
+   * zeros).  Required when the guard is on; frame_idx is optional otherwise. */
+  int32_t* loop_token;
+  int32_t* loop_run;
+  int32_t* loop_max_run;
+  int32_t* loop_suspect_count;
+  int32_t* loop_recovery_count;
+  int32_t* frame_idx;          /* +1 on every non-EOS row */
+  /* progress inputs [B] (required when the guard is on and min ratio > 0) */
+  const int32_t* decode_start_frame;
+  const int32_t* text_tokens_consumed;
+  const uint8_t* input_complete;
+
+  /* outputs (all optional) */
+  int32_t* events;             /* [B] Q3S_EVT_* bits */
+  int32_t* event_run;          /* [B] ended run on RECOVERED, run on an abort, else 0 */
+  int32_t* event_list;         /* [B] (row << 8) | bits for rows with any bit, ascending row */
+  int32_t* event_count;        /* one int32: entries written to event_list (required with it) */
+  int32_t* error_word;         /* Q3S_DEVERR_OFFSETS on bad offsets / capacity (row skipped) */
+} q3s_step_desc;
+
+/* One epilogue step over B rows; asynchronous on `stream`, no allocation. */
+q3s_status q3s_step_update(const q3s_step_desc* desc, void* stream);
 
 /* Kernel family for icdf steps that either family can serve (process-wide;
  * a tuning and test knob with no counterpart in the reference interface):

@@ -367,3 +367,114 @@ def cp_frame(base, *, mode: str, ids_init=None, rotate: bool = True, temperature
             bnd[:, j] = r["boundary"]
         prev = ids[:, j]
     return {"ids": ids, "boundary": bnd}
+
+
+# ---------------------------------------------------------------------------
+# per-step codec-0 epilogue: EOS, frame counter, token loop guard, history append
+# ---------------------------------------------------------------------------
+
+EVT_EOS, EVT_SUSPECT, EVT_RECOVERED, EVT_DEFERRED = 1, 2, 4, 8
+EVT_ABORT_PROGRESS, EVT_ABORT_EMERGENCY = 16, 32
+GUARD_FIELDS = ("loop_token", "loop_run", "loop_max_run", "loop_suspect_count", "loop_recovery_count", "frame_idx")
+
+
+def guard_thresholds(suspect: int, abort: int, emergency: int) -> tuple[int, int, int]:
+    """Threshold normalisation of EngineLoop.__init__
+    (engine/backend/engine_loop.py:372-387): abort clamped at 0; suspect kept
+    only with both stages on and then clamped to abort; emergency kept only
+    with both on and then raised to abort."""
+    abort = max(0, int(abort))
+    suspect = max(0, int(suspect))
+    suspect = min(suspect, abort) if suspect > 0 and abort > 0 else 0
+    emergency = max(0, int(emergency))
+    emergency = max(emergency, abort) if emergency > 0 and abort > 0 else 0
+    return suspect, abort, emergency
+
+
+def step_update(ids, *, eos_id: int, state: dict, suspect: int = 0, abort: int = 0, emergency: int = 0,
+                min_ratio: float = 0.0, decode_start_frame=None, text_tokens=None, input_complete=None,
+                history=None, offsets=None):
+    """One step of the per-row codec-0 epilogue, row by row.
+
+    * EOS: ``id == eos_id`` (engine/backend/executor.py:532-546); an EOS row
+      ends its segment and skips the guard (engine_loop.py:2838-2839).
+    * frame counter: ``frame_idx += 1`` on non-EOS rows, before the guard
+      (engine_loop.py:2749-2750).
+    * two-stage loop guard (engine_loop.py:2863-2966 and the decisions at
+      :2968-3080): run / recovery / suspect bookkeeping, the generation
+      progress gate ``audio_steps / text_tokens >= min_ratio`` (Python true
+      division of two ints = one correctly rounded double division), deferred
+      at ``run == abort`` without progress, abort by progress (confirmed) or
+      by the emergency stage.
+    * history append: row b of the packed history gains ``ids[b]`` (the packed
+      counterpart of ``token_counts + one_hot(id)``,
+      scripts/export/talker_unified_modules.py:421-422, applied to every row);
+      ``offsets_out[b] = offsets[b] + b``.
+
+    ``state`` maps GUARD_FIELDS to int arrays [B], updated in place.  Returns
+    (events [B] int32, run [B] int32 -- the ended run on RECOVERED, the run on
+    an abort, else 0 --, history_out or None, offsets_out or None).
+    """
+    ids = np.asarray(ids, np.int64)
+    B = ids.shape[0]
+    suspect, abort, emergency = guard_thresholds(suspect, abort, emergency)
+    min_ratio = max(0.0, float(min_ratio))
+    events = np.zeros(B, np.int32)
+    runs = np.zeros(B, np.int32)
+    st = {k: state[k] for k in GUARD_FIELDS}
+    for b in range(B):
+        tok = int(ids[b])
+        if tok == eos_id:
+            events[b] = EVT_EOS
+            continue
+        st["frame_idx"][b] += 1
+        if abort <= 0:
+            continue
+        bits = 0
+        if tok == st["loop_token"][b]:
+            st["loop_run"][b] += 1
+        else:
+            if suspect > 0 and st["loop_run"][b] >= suspect:
+                st["loop_recovery_count"][b] += 1
+                bits |= EVT_RECOVERED
+                runs[b] = st["loop_run"][b]
+            st["loop_token"][b] = tok
+            st["loop_run"][b] = 1
+        run = int(st["loop_run"][b])
+        st["loop_max_run"][b] = max(int(st["loop_max_run"][b]), run)
+        if suspect > 0 and run == suspect:
+            st["loop_suspect_count"][b] += 1
+            bits |= EVT_SUSPECT
+        audio_steps = max(0, int(st["frame_idx"][b]) - int(decode_start_frame[b] if decode_start_frame is not None else 0))
+        text = max(0, int(text_tokens[b] if text_tokens is not None else 0))
+        ratio = audio_steps / text if text > 0 else 0.0
+        complete = bool(input_complete[b]) if input_complete is not None else False
+        ready = min_ratio <= 0.0 or (complete and (text == 0 or ratio >= min_ratio))
+        confirmed = run >= abort and ready
+        emerg = emergency > 0 and run >= emergency
+        if run == abort and not ready:
+            bits |= EVT_DEFERRED
+        if confirmed:
+            bits |= EVT_ABORT_PROGRESS
+            runs[b] = run
+        elif emerg:
+            bits |= EVT_ABORT_EMERGENCY
+            runs[b] = run
+        events[b] = bits
+    hist_out = off_out = None
+    if history is not None:
+        history = np.asarray(history, np.int32)
+        offsets = np.asarray(offsets, np.int64)
+        off_out = (offsets + np.arange(B + 1)).astype(np.int32)
+        hist_out = np.empty(int(off_out[-1]), np.int32)
+        for b in range(B):
+            s, e = int(offsets[b]), int(offsets[b + 1])
+            hist_out[off_out[b]:off_out[b] + (e - s)] = history[s:e]
+            hist_out[off_out[b] + (e - s)] = ids[b]
+    return events, runs, hist_out, off_out
+
+
+def event_list(events: np.ndarray) -> np.ndarray:
+    """Rows with any event, ascending, packed as (row << 8) | bits."""
+    rows = np.nonzero(events)[0]
+    return ((rows.astype(np.int64) << 8) | events[rows]).astype(np.int32)

@@ -28,6 +28,7 @@
 #include "q3s_args.cuh"
 #include "q3s_device.cuh"
 #include "q3s_philox.cuh"
+#include "q3s_step.cuh"
 #include "q3s_sampler.h"
 
 namespace q3s {
@@ -1205,7 +1206,85 @@ q3s_status q3s_philox_rows(uint64_t seed, uint32_t step, const int64_t* row_keys
 uint32_t q3s_desc_size(int32_t which) {
   if (which == 0) return static_cast<uint32_t>(sizeof(q3s_sample_desc));
   if (which == 1) return static_cast<uint32_t>(sizeof(q3s_cp_frame_desc));
+  if (which == 2) return static_cast<uint32_t>(sizeof(q3s_step_desc));
   return 0;
+}
+
+q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
+  if (!d) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: desc is NULL");
+  if (d->struct_size != sizeof(q3s_step_desc))
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: struct_size %u != %u (ABI mismatch)", d->struct_size,
+                static_cast<unsigned>(sizeof(q3s_step_desc)));
+  const int B = d->batch;
+  if (B < 0 || B >= (1 << 23)) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: batch %d outside [0, 2^23)", B);
+  if (B == 0) return ok();
+  if ((d->ids_i64 == nullptr) == (d->ids_i32 == nullptr))
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: give exactly one of ids_i64 / ids_i32");
+  q3s::StepArgs a{};
+  a.batch = B;
+  a.eos_id = d->eos_id;
+  a.ids_i64 = d->ids_i64;
+  a.ids_i32 = d->ids_i32;
+  // threshold normalisation of EngineLoop.__init__ (engine/backend/engine_loop.py:372-387)
+  a.abort = std::max(0, d->abort_frames);
+  const int suspect = std::max(0, d->suspect_frames), emergency = std::max(0, d->emergency_frames);
+  a.suspect = (suspect > 0 && a.abort > 0) ? std::min(suspect, a.abort) : 0;
+  a.emergency = (emergency > 0 && a.abort > 0) ? std::max(emergency, a.abort) : 0;
+  const double ratio = d->min_audio_text_ratio;
+  if (ratio != ratio) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: min_audio_text_ratio is NaN");
+  a.min_ratio = ratio > 0.0 ? ratio : 0.0;
+  if (a.abort > 0) {
+    if (!d->loop_token || !d->loop_run || !d->loop_max_run || !d->loop_suspect_count || !d->loop_recovery_count)
+      return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: the loop guard is on but a guard state array is NULL");
+    if (a.min_ratio > 0.0 && (!d->frame_idx || !d->decode_start_frame || !d->text_tokens_consumed || !d->input_complete))
+      return fail(Q3S_ERR_INVALID_ARGUMENT,
+                  "q3s_step_update: the progress gate needs frame_idx, decode_start_frame, text_tokens_consumed and "
+                  "input_complete");
+  }
+  if (d->event_list && !d->event_count)
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: event_list needs event_count");
+  const bool append = d->history_out != nullptr;
+  if (append) {
+    if (!d->history || !d->offsets || !d->offsets_out)
+      return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: the history append needs history, offsets and offsets_out");
+    if (d->history_len < 0 || d->history_out_capacity < d->history_len + B || d->history_out_capacity > INT32_MAX)
+      return fail(Q3S_ERR_INVALID_ARGUMENT,
+                  "q3s_step_update: history_out_capacity %lld must lie in [history_len + batch, 2^31) (history_len %lld)",
+                  static_cast<long long>(d->history_out_capacity), static_cast<long long>(d->history_len));
+    const uintptr_t i0 = reinterpret_cast<uintptr_t>(d->history), i1 = i0 + 4 * static_cast<uintptr_t>(d->history_len);
+    const uintptr_t o0 = reinterpret_cast<uintptr_t>(d->history_out),
+                    o1 = o0 + 4 * static_cast<uintptr_t>(d->history_out_capacity);
+    if (i0 < o1 && o0 < i1)
+      return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: history_out overlaps history (rows shift right)");
+    const uintptr_t f0 = reinterpret_cast<uintptr_t>(d->offsets), f1 = f0 + 4 * static_cast<uintptr_t>(B + 1);
+    const uintptr_t g0 = reinterpret_cast<uintptr_t>(d->offsets_out), g1 = g0 + 4 * static_cast<uintptr_t>(B + 1);
+    if (f0 < g1 && g0 < f1) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: offsets_out overlaps offsets");
+  }
+  a.history = d->history;
+  a.offsets = d->offsets;
+  a.history_len = d->history_len;
+  a.history_out = d->history_out;
+  a.offsets_out = d->offsets_out;
+  a.history_out_capacity = d->history_out_capacity;
+  a.loop_token = d->loop_token;
+  a.loop_run = d->loop_run;
+  a.loop_max_run = d->loop_max_run;
+  a.loop_suspect_count = d->loop_suspect_count;
+  a.loop_recovery_count = d->loop_recovery_count;
+  a.frame_idx = d->frame_idx;
+  a.decode_start_frame = d->decode_start_frame;
+  a.text_tokens = d->text_tokens_consumed;
+  a.input_complete = d->input_complete;
+  a.events = d->events;
+  a.event_run = d->event_run;
+  a.event_list = d->event_list;
+  a.event_count = d->event_count;
+  a.error_word = d->error_word;
+  const unsigned grid = 1u + (append ? static_cast<unsigned>(B) : 0u);
+  q3s::step_update_kernel<<<grid, q3s::STEP_NT, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_step_update launch failed: %s", cudaGetErrorString(e));
+  return ok();
 }
 
 q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {

@@ -1,0 +1,223 @@
+// q3s_step.cuh -- the per-step codec-0 epilogue on the device (q3s_step_update).
+//
+// What it replaces (file:line in X-Square-Robot/Qwen3TTS-Streaming):
+//   EOS detection: the host reads every row's codebook-0 id back and compares
+//       it with the codec EOS id          engine/backend/executor.py:532-546
+//   frame counter: frame_idx += 1 on non-EOS rows, before the guard
+//                                         engine/backend/engine_loop.py:2749-2750
+//   two-stage token loop guard: run / recovery / suspect bookkeeping, the
+//       generation-progress gate, deferred / confirmed / emergency decisions
+//                                         engine/backend/engine_loop.py:2863-3080
+//   history append: the packed-history form of token_counts + one_hot(id)
+//                                         scripts/export/talker_unified_modules.py:421-422
+//
+// One launch, two roles:
+//   CTA 0          the guard for every row (STEP_RPT rows per thread per chunk,
+//                  their loads issued together), then an ordered compaction of
+//                  the rows with events into (row << 8) | bits and the count;
+//   CTA 1 + b      copies history row b to its shifted place in the output
+//                  (offsets_out[b] = offsets[b] + b) and appends ids[b].
+// Rows are independent and CTA 0 touches no history, so the roles need no
+// synchronisation between CTAs.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q3s_sampler.h"
+
+namespace q3s {
+
+constexpr int STEP_NT = 512;   // threads per CTA (both roles)
+constexpr int STEP_RPT = 4;    // guard rows per thread per chunk
+
+struct StepArgs {
+  int batch;
+  int eos_id;
+  const int64_t* ids_i64;
+  const int32_t* ids_i32;
+  const int32_t* history;
+  const int32_t* offsets;
+  int64_t history_len;
+  int32_t* history_out;
+  int32_t* offsets_out;
+  int64_t history_out_capacity;
+  int suspect, abort, emergency;  // normalised
+  double min_ratio;               // clamped at 0
+  int32_t* loop_token;
+  int32_t* loop_run;
+  int32_t* loop_max_run;
+  int32_t* loop_suspect_count;
+  int32_t* loop_recovery_count;
+  int32_t* frame_idx;
+  const int32_t* decode_start_frame;
+  const int32_t* text_tokens;
+  const uint8_t* input_complete;
+  int32_t* events;
+  int32_t* event_run;
+  int32_t* event_list;
+  int32_t* event_count;
+  int32_t* error_word;
+};
+
+__device__ __forceinline__ int64_t step_id(const StepArgs& a, int b) {
+  return a.ids_i64 ? a.ids_i64[b] : static_cast<int64_t>(a.ids_i32[b]);
+}
+
+// Per-row inputs of the guard, loaded together so one chunk's loads overlap.
+struct GuardRow {
+  int64_t id;
+  int frame, token, run, max_run, suspects, recoveries, start, text;
+  bool complete;
+};
+
+__device__ __forceinline__ void guard_load(const StepArgs& a, int b, GuardRow& r) {
+  r = GuardRow{};
+  r.id = step_id(a, b);
+  r.frame = a.frame_idx ? a.frame_idx[b] : 0;
+  if (a.abort > 0) {
+    r.token = a.loop_token[b];
+    r.run = a.loop_run[b];
+    r.max_run = a.loop_max_run[b];
+    r.suspects = a.loop_suspect_count[b];
+    r.recoveries = a.loop_recovery_count[b];
+    if (a.min_ratio > 0.0) {
+      r.start = a.decode_start_frame[b];
+      r.text = a.text_tokens[b];
+      r.complete = a.input_complete[b] != 0;
+    }
+  }
+}
+
+// The guard of one row (state written back); returns its event bits.
+__device__ __forceinline__ int guard_apply(const StepArgs& a, int b, GuardRow& r, int& ev_run) {
+  ev_run = 0;
+  if (r.id == a.eos_id) return Q3S_EVT_EOS;  // segment ends; no counter, no guard
+  r.frame += 1;
+  if (a.frame_idx) a.frame_idx[b] = r.frame;
+  if (a.abort <= 0) return 0;
+  int bits = 0;
+  if (r.id == static_cast<int64_t>(r.token)) {
+    r.run += 1;
+  } else {
+    if (a.suspect > 0 && r.run >= a.suspect) {
+      r.recoveries += 1;
+      bits |= Q3S_EVT_RECOVERED;
+      ev_run = r.run;
+    }
+    r.token = static_cast<int>(r.id);
+    r.run = 1;
+  }
+  r.max_run = max(r.max_run, r.run);
+  if (a.suspect > 0 && r.run == a.suspect) {
+    r.suspects += 1;
+    bits |= Q3S_EVT_SUSPECT;
+  }
+  bool ready = true;
+  if (a.min_ratio > 0.0) {
+    const int64_t steps = max(static_cast<int64_t>(0), static_cast<int64_t>(r.frame) - r.start);
+    const int text = max(0, r.text);
+    // Python's int / int: one correctly rounded double division (both exact).
+    const double ratio = text > 0 ? static_cast<double>(steps) / static_cast<double>(text) : 0.0;
+    ready = r.complete && (text == 0 || ratio >= a.min_ratio);
+  }
+  if (r.run == a.abort && !ready) bits |= Q3S_EVT_DEFERRED;
+  if (r.run >= a.abort && ready) {
+    bits |= Q3S_EVT_ABORT_PROGRESS;
+    ev_run = r.run;
+  } else if (a.emergency > 0 && r.run >= a.emergency) {
+    bits |= Q3S_EVT_ABORT_EMERGENCY;
+    ev_run = r.run;
+  }
+  a.loop_token[b] = r.token;
+  a.loop_run[b] = r.run;
+  a.loop_max_run[b] = r.max_run;
+  a.loop_suspect_count[b] = r.suspects;
+  a.loop_recovery_count[b] = r.recoveries;
+  return bits;
+}
+
+__device__ __forceinline__ void step_guard_cta(const StepArgs& a) {
+  __shared__ int cnt[STEP_RPT][STEP_NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned lt = (1u << lane) - 1u;
+  int base = 0;
+  for (int r0 = 0; r0 < a.batch; r0 += STEP_NT * STEP_RPT) {
+    GuardRow rows[STEP_RPT];
+#pragma unroll
+    for (int k = 0; k < STEP_RPT; ++k) {
+      const int b = r0 + k * STEP_NT + tid;
+      if (b < a.batch) guard_load(a, b, rows[k]);
+    }
+    int bits[STEP_RPT];
+    unsigned m[STEP_RPT];
+#pragma unroll
+    for (int k = 0; k < STEP_RPT; ++k) {
+      const int b = r0 + k * STEP_NT + tid;
+      bits[k] = 0;
+      if (b < a.batch) {
+        int ev_run;
+        bits[k] = guard_apply(a, b, rows[k], ev_run);
+        if (a.events) a.events[b] = bits[k];
+        if (a.event_run) a.event_run[b] = ev_run;
+      }
+      m[k] = __ballot_sync(0xffffffffu, bits[k] != 0);
+      if (lane == 0) cnt[k][warp] = __popc(m[k]);
+    }
+    __syncthreads();
+    // rows ascend k-major: all of k = 0 (by warp, lane), then k = 1, ...
+    int before = base;
+#pragma unroll
+    for (int k = 0; k < STEP_RPT; ++k) {
+      int pre = before;
+      for (int w = 0; w < warp; ++w) pre += cnt[k][w];
+      int tot = 0;
+      for (int w = 0; w < STEP_NT / 32; ++w) tot += cnt[k][w];
+      if (bits[k] && a.event_list) {
+        const int b = r0 + k * STEP_NT + tid;
+        a.event_list[pre + __popc(m[k] & lt)] = (b << 8) | bits[k];
+      }
+      before += tot;
+    }
+    base = before;
+    __syncthreads();  // cnt is rewritten by the next chunk
+  }
+  if (tid == 0 && a.event_count) *a.event_count = base;
+}
+
+// History row b -> history_out[offsets[b] + b ...], then ids[b].
+__device__ __forceinline__ void step_append_cta(const StepArgs& a, int b) {
+  const int64_t s = a.offsets[b], e = a.offsets[b + 1];
+  const int64_t d = s + b, n = e - s;
+  if (threadIdx.x == 0) {
+    a.offsets_out[b] = static_cast<int32_t>(d);
+    if (b == a.batch - 1) a.offsets_out[a.batch] = static_cast<int32_t>(e + a.batch);
+  }
+  const bool ok = s >= 0 && n >= 0 && e <= a.history_len && d + n + 1 <= a.history_out_capacity;
+  if (!ok) {
+    if (threadIdx.x == 0 && a.error_word) atomicOr(a.error_word, Q3S_DEVERR_OFFSETS);
+    return;
+  }
+  const int32_t* src = a.history + s;
+  int32_t* dst = a.history_out + d;
+  int64_t i = threadIdx.x;
+  for (; i + 3 * STEP_NT < n; i += 4 * STEP_NT) {
+    const int32_t v0 = __ldcs(src + i), v1 = __ldcs(src + i + STEP_NT);
+    const int32_t v2 = __ldcs(src + i + 2 * STEP_NT), v3 = __ldcs(src + i + 3 * STEP_NT);
+    dst[i] = v0;
+    dst[i + STEP_NT] = v1;
+    dst[i + 2 * STEP_NT] = v2;
+    dst[i + 3 * STEP_NT] = v3;
+  }
+  for (; i < n; i += STEP_NT) dst[i] = __ldcs(src + i);
+  if (threadIdx.x == 0) dst[n] = static_cast<int32_t>(step_id(a, b));
+}
+
+__global__ void __launch_bounds__(STEP_NT) step_update_kernel(const StepArgs a) {
+  if (blockIdx.x == 0)
+    step_guard_cta(a);
+  else
+    step_append_cta(a, static_cast<int>(blockIdx.x) - 1);
+}
+
+}  // namespace q3s

@@ -4,6 +4,7 @@ Python host side over the C ABI of ``include/q3s_sampler.h``; the sampling
 itself runs only in the sm_100a kernels of ``libq3s_sampler.so``.
 """
 from . import _lib
+from .step import StepGuard, step_update
 from .ops import (
     CodecSampler,
     CpFramePlan,
@@ -23,6 +24,8 @@ __all__ = [
     "CodecSampler",
     "CpFramePlan",
     "SamplePlan",
+    "StepGuard",
+    "step_update",
     "kernel_policy",
     "philox_rows",
     "sample_codebook0",

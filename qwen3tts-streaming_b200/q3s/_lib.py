@@ -103,6 +103,45 @@ class CpFrameDesc(C.Structure):
     ]
 
 
+EVT_EOS, EVT_SUSPECT, EVT_RECOVERED, EVT_DEFERRED, EVT_ABORT_PROGRESS, EVT_ABORT_EMERGENCY = 1, 2, 4, 8, 16, 32
+
+
+class StepDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("batch", C.c_int32),
+        ("ids_i64", _p),
+        ("ids_i32", _p),
+        ("eos_id", C.c_int32),
+        ("reserved0", C.c_int32),
+        ("history", _p),
+        ("offsets", _p),
+        ("history_len", C.c_int64),
+        ("history_out", _p),
+        ("offsets_out", _p),
+        ("history_out_capacity", C.c_int64),
+        ("suspect_frames", C.c_int32),
+        ("abort_frames", C.c_int32),
+        ("emergency_frames", C.c_int32),
+        ("reserved1", C.c_int32),
+        ("min_audio_text_ratio", C.c_double),
+        ("loop_token", _p),
+        ("loop_run", _p),
+        ("loop_max_run", _p),
+        ("loop_suspect_count", _p),
+        ("loop_recovery_count", _p),
+        ("frame_idx", _p),
+        ("decode_start_frame", _p),
+        ("text_tokens_consumed", _p),
+        ("input_complete", _p),
+        ("events", _p),
+        ("event_run", _p),
+        ("event_list", _p),
+        ("event_count", _p),
+        ("error_word", _p),
+    ]
+
+
 # every symbol include/q3s_sampler.h declares
 EXPORTS = (
     "q3s_sample",
@@ -112,6 +151,7 @@ EXPORTS = (
     "q3s_desc_size",
     "q3s_set_kernel_policy",
     "q3s_philox_rows",
+    "q3s_step_update",
 )
 
 _lock = threading.Lock()
@@ -145,9 +185,11 @@ def load(path: str | Path | None = None) -> C.CDLL:
         lib.q3s_philox_rows.argtypes = [C.c_uint64, C.c_uint32, _p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                         _p, C.c_int64, _p]
         lib.q3s_philox_rows.restype = C.c_int
+        lib.q3s_step_update.argtypes = [C.POINTER(StepDesc), _p]
+        lib.q3s_step_update.restype = C.c_int
         if lib.q3s_abi_version() != Q3S_ABI_VERSION:
             raise RuntimeError(f"q3s ABI {lib.q3s_abi_version()} != binding {Q3S_ABI_VERSION}; rebuild")
-        for which, st in ((0, SampleDesc), (1, CpFrameDesc)):
+        for which, st in ((0, SampleDesc), (1, CpFrameDesc), (2, StepDesc)):
             if lib.q3s_desc_size(which) != C.sizeof(st):
                 raise RuntimeError(f"q3s descriptor {st.__name__} size {C.sizeof(st)} != library "
                                    f"{lib.q3s_desc_size(which)}; rebuild")

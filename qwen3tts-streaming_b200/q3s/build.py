@@ -18,7 +18,7 @@ CSRC = ROOT / "csrc"
 INCLUDE = REPO / "include"
 LIB_PATH = PKG_DIR / "libq3s_sampler.so"
 SOURCES = [CSRC / "q3s_sampler.cu", CSRC / "q3s_warp.cu"]
-DEPS = SOURCES + [CSRC / "q3s_args.cuh", CSRC / "q3s_device.cuh", CSRC / "q3s_warp.cuh", CSRC / "q3s_philox.cuh",
+DEPS = SOURCES + [CSRC / "q3s_args.cuh", CSRC / "q3s_device.cuh", CSRC / "q3s_warp.cuh", CSRC / "q3s_philox.cuh", CSRC / "q3s_step.cuh",
                   INCLUDE / "q3s_sampler.h"]
 
 NVCC_FLAGS = [

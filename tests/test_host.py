@@ -104,6 +104,7 @@ def test_library_exports_every_declared_symbol(lib):
     assert lib.q3s_abi_version() == _lib.Q3S_ABI_VERSION
     assert lib.q3s_desc_size(0) == C.sizeof(_lib.SampleDesc)
     assert lib.q3s_desc_size(1) == C.sizeof(_lib.CpFrameDesc)
+    assert lib.q3s_desc_size(2) == C.sizeof(_lib.StepDesc)
 
 
 def _desc(**kw):
@@ -170,6 +171,50 @@ def test_cp_frame_rejects_bad_arguments(lib):
     d.stages = 15
     d.logits_stage_stride = 100
     assert lib.q3s_sample_cp_frame(C.byref(d), None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def _step_desc(**kw):
+    d = _lib.StepDesc()
+    d.struct_size = C.sizeof(_lib.StepDesc)
+    d.batch, d.eos_id, d.ids_i64 = 4, 2150, 0x1000
+    d.suspect_frames, d.abort_frames, d.emergency_frames, d.min_audio_text_ratio = 4, 10, 20, 2.0
+    d.loop_token, d.loop_run, d.loop_max_run = 0x2000, 0x2100, 0x2200
+    d.loop_suspect_count, d.loop_recovery_count, d.frame_idx = 0x2300, 0x2400, 0x2500
+    d.decode_start_frame, d.text_tokens_consumed, d.input_complete = 0x2600, 0x2700, 0x2800
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(struct_size=8), "struct_size"),
+    (dict(batch=-1), "batch"),
+    (dict(batch=1 << 23), "batch"),
+    (dict(ids_i64=None), "exactly one"),
+    (dict(ids_i32=0x1100), "exactly one"),
+    (dict(loop_run=None), "guard state"),
+    (dict(input_complete=None), "progress gate"),
+    (dict(min_audio_text_ratio=float("nan")), "NaN"),
+    (dict(event_list=0x3000), "event_count"),
+    (dict(history_out=0x4000), "needs history"),
+    (dict(history_out=0x4000, history=0x5000, offsets=0x6000, offsets_out=0x7000, history_len=100,
+          history_out_capacity=103), "capacity"),
+    (dict(history_out=0x5010, history=0x5000, offsets=0x6000, offsets_out=0x7000, history_len=100,
+          history_out_capacity=104), "overlaps history"),
+    (dict(history_out=0x9000, history=0x5000, offsets=0x6000, offsets_out=0x6008, history_len=100,
+          history_out_capacity=104), "overlaps offsets"),
+])
+def test_step_update_rejects_bad_arguments_on_host(lib, kw, msg):
+    d = _step_desc(**kw)
+    assert lib.q3s_step_update(C.byref(d), None) == _lib.ERR_INVALID_ARGUMENT
+    assert msg in lib.q3s_last_error_string().decode()
+
+
+def test_step_update_guard_off_and_empty_batch(lib):
+    assert lib.q3s_step_update(None, None) == _lib.ERR_INVALID_ARGUMENT
+    # guard off (abort <= 0): the state arrays are not needed; batch 0 is a no-op
+    d = _step_desc(batch=0, abort_frames=0, loop_run=None, input_complete=None)
+    assert lib.q3s_step_update(C.byref(d), None) == _lib.OK
 
 
 def test_python_api_refuses_cpu_tensors():

@@ -121,3 +121,62 @@ def test_cp_frame_chain_depends_on_previous_ids():
         prev = init if j == 0 else a[:, j - 1]
         np.testing.assert_array_equal(a[:, j], O.rotate_rows(base[j], prev).argmax(-1))
     assert torch.is_tensor(torch.from_numpy(a))
+
+
+# ---- per-step epilogue: EOS, frame counter, loop guard (reference engine loop) ----
+
+def _replay_guard(g, i, fn):
+    """Feed scenario i of guard_steps.npz step by step through ``fn`` and
+    compare events, event runs and state with what the reference engine loop
+    recorded (rows compared while they are active; state of rows the step
+    ended is not compared)."""
+    su, ab, ra, em = g["scenarios"][i]
+    c, tok, act = g[f"s{i}_consts"], g[f"s{i}_tokens"], g[f"s{i}_active"].astype(bool)
+    S = c.shape[0]
+    state = {k: np.zeros(S, np.int64) for k in O.GUARD_FIELDS}
+    state["loop_token"][:] = -1
+    state["frame_idx"][:] = c[:, 0]
+    cfg = dict(suspect=int(su), abort=int(ab), emergency=int(em), min_ratio=float(ra), decode_start_frame=c[:, 1],
+               text_tokens=c[:, 2], input_complete=c[:, 3])
+    for t in range(tok.shape[0]):
+        ev, runs = fn(tok[t], state, cfg)
+        a = act[t]
+        np.testing.assert_array_equal(ev[a], g[f"s{i}_events"][t][a], err_msg=f"scenario {i} step {t}")
+        np.testing.assert_array_equal(runs[a], g[f"s{i}_runs"][t][a], err_msg=f"scenario {i} step {t}")
+        live = a & ((g[f"s{i}_events"][t] & (O.EVT_EOS | O.EVT_ABORT_PROGRESS | O.EVT_ABORT_EMERGENCY)) == 0)
+        st = np.stack([state[k] for k in O.GUARD_FIELDS], 1)
+        np.testing.assert_array_equal(st[live], g[f"s{i}_state"][t][live], err_msg=f"scenario {i} step {t}")
+
+
+def test_step_guard_oracle_matches_reference_engine_loop():
+    g = load_golden("guard_steps")
+    seen = 0
+    for i in range(len(g["scenarios"])):
+        def fn(ids, state, cfg):
+            ev, runs, _, _ = O.step_update(ids, eos_id=int(g["eos_id"]), state=state, **cfg)
+            return ev, runs
+        _replay_guard(g, i, fn)
+        seen |= int(np.bitwise_or.reduce(g[f"s{i}_events"].ravel()))
+    assert seen == 63  # every event kind occurs in the fixture
+
+
+def test_step_guard_thresholds_normalised_like_engine():
+    assert O.guard_thresholds(4, 10, 20) == (4, 10, 20)
+    assert O.guard_thresholds(9, 5, 3) == (5, 5, 5)
+    assert O.guard_thresholds(4, 0, 20) == (0, 0, 0)
+    assert O.guard_thresholds(-1, 6, -2) == (0, 6, 0)
+
+
+def test_step_history_append_oracle():
+    rng = np.random.default_rng(3)
+    lens = rng.integers(0, 9, 7)
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    hist = rng.integers(0, 3072, offs[-1]).astype(np.int32)
+    ids = rng.integers(0, 3072, 7)
+    state = {k: np.zeros(7, np.int64) for k in O.GUARD_FIELDS}
+    _, _, h2, o2 = O.step_update(ids, eos_id=2150, state=state, history=hist, offsets=offs)
+    for b in range(7):
+        row = h2[o2[b]:o2[b + 1]]
+        np.testing.assert_array_equal(row[:-1], hist[offs[b]:offs[b + 1]])
+        assert row[-1] == ids[b]
+    assert o2[-1] == offs[-1] + 7
