@@ -228,7 +228,7 @@ typedef struct q3s_step_desc {
   /* packed history append (history_out NULL = skipped).  Row b of the output
    * is row b of the input followed by ids[b]; offsets_out[b] = offsets[b] + b.
    * history_out must not overlap history. */
-  const int32_t* history;      /* packed ids; row b = history[offsets[b] .. offsets[b+1]) */
+  const int32_t* history;      /* packed ids (NULL allowed when history_len is 0); row b = history[offsets[b] .. offsets[b+1]) */
   const int32_t* offsets;      /* [B+1] */
   int64_t history_len;         /* entries in `history` (bounds check) */
   int32_t* history_out;        /* capacity history_out_capacity entries (>= history_len + B) */

@@ -1245,8 +1245,9 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: event_list needs event_count");
   const bool append = d->history_out != nullptr;
   if (append) {
-    if (!d->history || !d->offsets || !d->offsets_out)
-      return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: the history append needs history, offsets and offsets_out");
+    if ((!d->history && d->history_len > 0) || !d->offsets || !d->offsets_out)
+      return fail(Q3S_ERR_INVALID_ARGUMENT,
+                  "q3s_step_update: the history append needs history (unless empty), offsets and offsets_out");
     if (d->history_len < 0 || d->history_out_capacity < d->history_len + B || d->history_out_capacity > INT32_MAX)
       return fail(Q3S_ERR_INVALID_ARGUMENT,
                   "q3s_step_update: history_out_capacity %lld must lie in [history_len + batch, 2^31) (history_len %lld)",
