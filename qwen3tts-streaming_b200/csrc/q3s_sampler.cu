@@ -1281,8 +1281,9 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
   a.event_list = d->event_list;
   a.event_count = d->event_count;
   a.error_word = d->error_word;
-  const unsigned grid = 1u + (append ? static_cast<unsigned>(B) : 0u);
-  q3s::step_update_kernel<<<grid, q3s::STEP_NT, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (append) q3s::step_append_kernel<<<static_cast<unsigned>(B), q3s::APPEND_NT, 0, st>>>(a);
+  q3s::step_guard_kernel<<<1, q3s::STEP_NT, 0, st>>>(a);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_step_update launch failed: %s", cudaGetErrorString(e));
   return ok();

@@ -11,14 +11,17 @@
 //   history append: the packed-history form of token_counts + one_hot(id)
 //                                         scripts/export/talker_unified_modules.py:421-422
 //
-// One launch, two roles:
-//   CTA 0          the guard for every row (STEP_RPT rows per thread per chunk,
-//                  their loads issued together), then an ordered compaction of
-//                  the rows with events into (row << 8) | bits and the count;
-//   CTA 1 + b      copies history row b to its shifted place in the output
-//                  (offsets_out[b] = offsets[b] + b) and appends ids[b].
-// Rows are independent and CTA 0 touches no history, so the roles need no
-// synchronisation between CTAs.
+// Two launches on the caller's stream:
+//   step_append_kernel  CTA b copies history row b to its shifted place in the
+//                       output (offsets_out[b] = offsets[b] + b) and appends
+//                       ids[b]; register-light so 8 CTAs stay resident per SM;
+//   step_guard_kernel   one CTA: the guard for every row (STEP_RPT rows per
+//                       thread per chunk, their loads issued together), then an
+//                       ordered compaction of the rows with events into
+//                       (row << 8) | bits and the count.
+// The guard's per-row register state would cap the copy at one CTA per SM if
+// both roles shared a kernel, so they are launched apart; neither reads what
+// the other writes.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -185,8 +188,15 @@ __device__ __forceinline__ void step_guard_cta(const StepArgs& a) {
   if (tid == 0 && a.event_count) *a.event_count = base;
 }
 
-// History row b -> history_out[offsets[b] + b ...], then ids[b].
-__device__ __forceinline__ void step_append_cta(const StepArgs& a, int b) {
+// History row b -> history_out[offsets[b] + b ...], then ids[b].  One CTA of
+// APPEND_NT threads per row, APPEND_U loads in flight per thread; the kernel
+// is held to 32 registers so 8 CTAs (2048 threads) stay resident per SM and
+// enough rows are in flight to cover DRAM latency.
+constexpr int APPEND_NT = 256;
+constexpr int APPEND_U = 8;
+
+__global__ void __launch_bounds__(APPEND_NT, 8) step_append_kernel(const StepArgs a) {
+  const int b = blockIdx.x;
   const int64_t s = a.offsets[b], e = a.offsets[b + 1];
   const int64_t d = s + b, n = e - s;
   if (threadIdx.x == 0) {
@@ -200,24 +210,24 @@ __device__ __forceinline__ void step_append_cta(const StepArgs& a, int b) {
   }
   const int32_t* src = a.history + s;
   int32_t* dst = a.history_out + d;
-  int64_t i = threadIdx.x;
-  for (; i + 3 * STEP_NT < n; i += 4 * STEP_NT) {
-    const int32_t v0 = __ldcs(src + i), v1 = __ldcs(src + i + STEP_NT);
-    const int32_t v2 = __ldcs(src + i + 2 * STEP_NT), v3 = __ldcs(src + i + 3 * STEP_NT);
-    dst[i] = v0;
-    dst[i + STEP_NT] = v1;
-    dst[i + 2 * STEP_NT] = v2;
-    dst[i + 3 * STEP_NT] = v3;
+  const int n32 = static_cast<int>(n);  // n <= history_len < 2^31 (checked on the host)
+  for (int i0 = 0; i0 < n32; i0 += APPEND_U * APPEND_NT) {
+    int32_t v[APPEND_U];
+#pragma unroll
+    for (int u = 0; u < APPEND_U; ++u) {
+      const int i = i0 + u * APPEND_NT + static_cast<int>(threadIdx.x);
+      if (i < n32) v[u] = __ldcs(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < APPEND_U; ++u) {
+      const int i = i0 + u * APPEND_NT + static_cast<int>(threadIdx.x);
+      if (i < n32) dst[i] = v[u];
+    }
   }
-  for (; i < n; i += STEP_NT) dst[i] = __ldcs(src + i);
   if (threadIdx.x == 0) dst[n] = static_cast<int32_t>(step_id(a, b));
 }
 
-__global__ void __launch_bounds__(STEP_NT) step_update_kernel(const StepArgs a) {
-  if (blockIdx.x == 0)
-    step_guard_cta(a);
-  else
-    step_append_cta(a, static_cast<int>(blockIdx.x) - 1);
-}
+// The guard of all rows in one CTA (ordered event list needs one CTA).
+__global__ void __launch_bounds__(STEP_NT) step_guard_kernel(const StepArgs a) { step_guard_cta(a); }
 
 }  // namespace q3s
