@@ -207,9 +207,10 @@ q3s_status q3s_philox_rows(uint64_t seed, uint32_t step, const int64_t* row_keys
  * id back to the host each step (engine/backend/executor.py:532-546) and runs
  * these checks per slot in Python (engine/backend/engine_loop.py:2749-2750,
  * 2863-3080, thresholds normalised at :372-387); the count update it feeds is
- * talker_unified_modules.py:421-422.  One launch does them for all rows and
- * leaves a compact event list, so the host reads one word per step (the event
- * count) and the listed rows only when it is non-zero. */
+ * talker_unified_modules.py:421-422.  Two kernel launches do them for all
+ * rows (per-row guard + history copy, then the event compaction when asked
+ * for) and leave a compact event list, so the host reads one word per step
+ * (the event count) and the listed rows only when it is non-zero. */
 #define Q3S_EVT_EOS 1              /* id == eos_id: segment ends, guard skipped */
 #define Q3S_EVT_SUSPECT 2          /* loop_run reached the suspect threshold */
 #define Q3S_EVT_RECOVERED 4        /* token changed after a run >= suspect */
@@ -258,7 +259,7 @@ typedef struct q3s_step_desc {
   const uint8_t* input_complete;
 
   /* outputs (all optional) */
-  int32_t* events;             /* [B] Q3S_EVT_* bits */
+  int32_t* events;             /* [B] Q3S_EVT_* bits (required with event_list / event_count) */
   int32_t* event_run;          /* [B] ended run on RECOVERED, run on an abort, else 0 */
   int32_t* event_list;         /* [B] (row << 8) | bits for rows with any bit, ascending row */
   int32_t* event_count;        /* one int32: entries written to event_list (required with it) */

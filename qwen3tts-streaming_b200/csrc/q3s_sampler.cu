@@ -1243,6 +1243,8 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
   }
   if (d->event_list && !d->event_count)
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: event_list needs event_count");
+  if (d->event_count && !d->events)
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: event_list / event_count are compacted from events");
   const bool append = d->history_out != nullptr;
   if (append) {
     if ((!d->history && d->history_len > 0) || !d->offsets || !d->offsets_out)
@@ -1282,8 +1284,8 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
   a.event_count = d->event_count;
   a.error_word = d->error_word;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (append) q3s::step_append_kernel<<<static_cast<unsigned>(B), q3s::APPEND_NT, 0, st>>>(a);
-  q3s::step_guard_kernel<<<1, q3s::STEP_NT, 0, st>>>(a);
+  q3s::step_rows_kernel<<<static_cast<unsigned>(B), append ? q3s::APPEND_NT : 32, 0, st>>>(a);
+  if (d->event_list || d->event_count) q3s::step_compact_kernel<<<1, q3s::COMPACT_NT, 0, st>>>(a);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_step_update launch failed: %s", cudaGetErrorString(e));
   return ok();

@@ -12,16 +12,14 @@
 //                                         scripts/export/talker_unified_modules.py:421-422
 //
 // Two launches on the caller's stream:
-//   step_append_kernel  CTA b copies history row b to its shifted place in the
-//                       output (offsets_out[b] = offsets[b] + b) and appends
-//                       ids[b]; register-light so 8 CTAs stay resident per SM;
-//   step_guard_kernel   one CTA: the guard for every row (STEP_RPT rows per
-//                       thread per chunk, their loads issued together), then an
-//                       ordered compaction of the rows with events into
-//                       (row << 8) | bits and the count.
-// The guard's per-row register state would cap the copy at one CTA per SM if
-// both roles shared a kernel, so they are launched apart; neither reads what
-// the other writes.
+//   step_rows_kernel     CTA b: thread 0 runs row b's guard (events[b],
+//                        event_run[b], state) while the CTA copies history row
+//                        b to its shifted place in the output
+//                        (offsets_out[b] = offsets[b] + b) and appends ids[b];
+//                        register-light so 8 CTAs stay resident per SM;
+//   step_compact_kernel  one CTA: ordered compaction of events[] into
+//                        (row << 8) | bits entries and the count (only when
+//                        the caller asks for the list or the count).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -30,9 +28,6 @@
 #include "q3s_sampler.h"
 
 namespace q3s {
-
-constexpr int STEP_NT = 512;   // threads per CTA (both roles)
-constexpr int STEP_RPT = 4;    // guard rows per thread per chunk
 
 struct StepArgs {
   int batch;
@@ -67,7 +62,7 @@ __device__ __forceinline__ int64_t step_id(const StepArgs& a, int b) {
   return a.ids_i64 ? a.ids_i64[b] : static_cast<int64_t>(a.ids_i32[b]);
 }
 
-// Per-row inputs of the guard, loaded together so one chunk's loads overlap.
+// Per-row inputs of the guard.
 struct GuardRow {
   int64_t id;
   int frame, token, run, max_run, suspects, recoveries, start, text;
@@ -140,63 +135,25 @@ __device__ __forceinline__ int guard_apply(const StepArgs& a, int b, GuardRow& r
   return bits;
 }
 
-__device__ __forceinline__ void step_guard_cta(const StepArgs& a) {
-  __shared__ int cnt[STEP_RPT][STEP_NT / 32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const unsigned lt = (1u << lane) - 1u;
-  int base = 0;
-  for (int r0 = 0; r0 < a.batch; r0 += STEP_NT * STEP_RPT) {
-    GuardRow rows[STEP_RPT];
-#pragma unroll
-    for (int k = 0; k < STEP_RPT; ++k) {
-      const int b = r0 + k * STEP_NT + tid;
-      if (b < a.batch) guard_load(a, b, rows[k]);
-    }
-    int bits[STEP_RPT];
-    unsigned m[STEP_RPT];
-#pragma unroll
-    for (int k = 0; k < STEP_RPT; ++k) {
-      const int b = r0 + k * STEP_NT + tid;
-      bits[k] = 0;
-      if (b < a.batch) {
-        int ev_run;
-        bits[k] = guard_apply(a, b, rows[k], ev_run);
-        if (a.events) a.events[b] = bits[k];
-        if (a.event_run) a.event_run[b] = ev_run;
-      }
-      m[k] = __ballot_sync(0xffffffffu, bits[k] != 0);
-      if (lane == 0) cnt[k][warp] = __popc(m[k]);
-    }
-    __syncthreads();
-    // rows ascend k-major: all of k = 0 (by warp, lane), then k = 1, ...
-    int before = base;
-#pragma unroll
-    for (int k = 0; k < STEP_RPT; ++k) {
-      int pre = before;
-      for (int w = 0; w < warp; ++w) pre += cnt[k][w];
-      int tot = 0;
-      for (int w = 0; w < STEP_NT / 32; ++w) tot += cnt[k][w];
-      if (bits[k] && a.event_list) {
-        const int b = r0 + k * STEP_NT + tid;
-        a.event_list[pre + __popc(m[k] & lt)] = (b << 8) | bits[k];
-      }
-      before += tot;
-    }
-    base = before;
-    __syncthreads();  // cnt is rewritten by the next chunk
-  }
-  if (tid == 0 && a.event_count) *a.event_count = base;
-}
-
-// History row b -> history_out[offsets[b] + b ...], then ids[b].  One CTA of
-// APPEND_NT threads per row, APPEND_U loads in flight per thread; the kernel
-// is held to 32 registers so 8 CTAs (2048 threads) stay resident per SM and
-// enough rows are in flight to cover DRAM latency.
+// History row b -> history_out[offsets[b] + b ...], then ids[b]; thread 0
+// runs row b's guard meanwhile.  One CTA of APPEND_NT threads per row,
+// APPEND_U loads in flight per thread; held to 32 registers so 8 CTAs (2048
+// threads) stay resident per SM and enough rows are in flight to cover DRAM
+// latency.  Without the append the CTA is one warp and only the guard runs.
 constexpr int APPEND_NT = 256;
 constexpr int APPEND_U = 8;
 
-__global__ void __launch_bounds__(APPEND_NT, 8) step_append_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(APPEND_NT, 8) step_rows_kernel(const StepArgs a) {
   const int b = blockIdx.x;
+  if (threadIdx.x == 0) {
+    GuardRow r;
+    guard_load(a, b, r);
+    int ev_run;
+    const int bits = guard_apply(a, b, r, ev_run);
+    if (a.events) a.events[b] = bits;
+    if (a.event_run) a.event_run[b] = ev_run;
+  }
+  if (!a.history_out) return;
   const int64_t s = a.offsets[b], e = a.offsets[b + 1];
   const int64_t d = s + b, n = e - s;
   if (threadIdx.x == 0) {
@@ -227,7 +184,49 @@ __global__ void __launch_bounds__(APPEND_NT, 8) step_append_kernel(const StepArg
   if (threadIdx.x == 0) dst[n] = static_cast<int32_t>(step_id(a, b));
 }
 
-// The guard of all rows in one CTA (ordered event list needs one CTA).
-__global__ void __launch_bounds__(STEP_NT) step_guard_kernel(const StepArgs a) { step_guard_cta(a); }
+// Ordered compaction of events[0, B) into event_list ((row << 8) | bits for
+// rows with any bit, ascending) and event_count.  One CTA: thread t takes
+// COMPACT_RPT consecutive rows of each chunk, so thread order is row order and
+// one block scan of per-thread counts places every entry.
+constexpr int COMPACT_NT = 1024;
+constexpr int COMPACT_RPT = 4;
+
+__global__ void __launch_bounds__(COMPACT_NT) step_compact_kernel(const StepArgs a) {
+  __shared__ int warp_tot[COMPACT_NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int base = 0;
+  for (int r0 = 0; r0 < a.batch; r0 += COMPACT_NT * COMPACT_RPT) {
+    const int b0 = r0 + tid * COMPACT_RPT;
+    int ev[COMPACT_RPT];
+    int c = 0;
+#pragma unroll
+    for (int k = 0; k < COMPACT_RPT; ++k) {
+      ev[k] = b0 + k < a.batch ? a.events[b0 + k] : 0;
+      c += ev[k] != 0;
+    }
+    int incl = c;  // inclusive warp scan of the per-thread counts
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int pre = base + incl - c, tot = 0;
+    for (int w = 0; w < COMPACT_NT / 32; ++w) {
+      const int t = warp_tot[w];
+      pre += w < warp ? t : 0;
+      tot += t;
+    }
+    if (a.event_list) {
+#pragma unroll
+      for (int k = 0; k < COMPACT_RPT; ++k)
+        if (ev[k]) a.event_list[pre++] = ((b0 + k) << 8) | ev[k];
+    }
+    base += tot;
+    __syncthreads();  // warp_tot is rewritten by the next chunk
+  }
+  if (tid == 0 && a.event_count) *a.event_count = base;
+}
 
 }  // namespace q3s

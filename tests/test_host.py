@@ -196,6 +196,7 @@ def _step_desc(**kw):
     (dict(input_complete=None), "progress gate"),
     (dict(min_audio_text_ratio=float("nan")), "NaN"),
     (dict(event_list=0x3000), "event_count"),
+    (dict(event_list=0x3000, event_count=0x3100), "compacted from events"),
     (dict(history_out=0x4000), "needs history"),
     (dict(history_out=0x4000, history=0x5000, offsets=0x6000, offsets_out=0x7000, history_len=100,
           history_out_capacity=103), "capacity"),
