@@ -180,3 +180,45 @@ def test_step_history_append_oracle():
         np.testing.assert_array_equal(row[:-1], hist[offs[b]:offs[b + 1]])
         assert row[-1] == ids[b]
     assert o2[-1] == offs[-1] + 7
+
+
+def test_step_update_shards_by_rows():
+    """Rows are independent: running the epilogue per rank on its row block
+    (q3s.shard.row_range, offsets rebased) and shifting each rank's event rows
+    by its first row reproduces the single-batch events, state and history."""
+    from q3s import shard
+
+    rng = np.random.default_rng(11)
+    B, world = 37, 4
+    lens = rng.integers(0, 20, B)
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    hist = rng.integers(0, 3072, offs[-1]).astype(np.int32)
+    cfg = dict(suspect=2, abort=3, emergency=5, min_ratio=1.0, decode_start_frame=rng.integers(0, 5, B),
+               text_tokens=rng.integers(0, 4, B), input_complete=rng.integers(0, 2, B))
+
+    def fresh(n):
+        st = {k: np.zeros(n, np.int64) for k in O.GUARD_FIELDS}
+        st["loop_token"][:] = -1
+        return st
+
+    full, parts = fresh(B), [fresh(shard.row_range(r, world, B)[1] - shard.row_range(r, world, B)[0])
+                             for r in range(world)]
+    for _ in range(6):
+        ids = np.where(rng.random(B) < 0.1, 2150, rng.integers(0, 3, B) + 500)
+        ev, runs, h_full, o_full = O.step_update(ids, eos_id=2150, state=full, history=hist, offsets=offs, **cfg)
+        got_list, got_hist = [], []
+        for r in range(world):
+            a, b = shard.row_range(r, world, B)
+            sub = {k: (v[a:b] if isinstance(v, np.ndarray) else v) for k, v in cfg.items()}
+            o = offs[a:b + 1] - offs[a]
+            e, ru, h, _ = O.step_update(ids[a:b], eos_id=2150, state=parts[r], history=hist[offs[a]:offs[b]],
+                                        offsets=o, **sub)
+            np.testing.assert_array_equal(e, ev[a:b])
+            np.testing.assert_array_equal(ru, runs[a:b])
+            for k in O.GUARD_FIELDS:
+                np.testing.assert_array_equal(parts[r][k], full[k][a:b])
+            got_list += [(int(v) >> 8) + a for v in O.event_list(e)]
+            got_hist.append(h)
+        assert got_list == [int(v) >> 8 for v in O.event_list(ev)]
+        np.testing.assert_array_equal(np.concatenate(got_hist), h_full)
+        hist, offs = h_full, o_full.astype(np.int64)
