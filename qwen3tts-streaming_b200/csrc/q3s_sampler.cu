@@ -1285,8 +1285,21 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
   a.error_word = d->error_word;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   q3s::step_rows_kernel<<<static_cast<unsigned>(B), append ? q3s::APPEND_NT : 32, 0, st>>>(a);
-  if (d->event_list || d->event_count) q3s::step_compact_kernel<<<1, q3s::COMPACT_NT, 0, st>>>(a);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && (d->event_list || d->event_count)) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(1);
+    lc.blockDim = dim3(q3s::COMPACT_NT);
+    lc.dynamicSmemBytes = 0;
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&lc, q3s::step_compact_kernel, a);
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_step_update launch failed: %s", cudaGetErrorString(e));
   return ok();
 }

@@ -19,7 +19,9 @@
 //                        register-light so 8 CTAs stay resident per SM;
 //   step_compact_kernel  one CTA: ordered compaction of events[] into
 //                        (row << 8) | bits entries and the count (only when
-//                        the caller asks for the list or the count).
+//                        the caller asks for the list or the count); a
+//                        programmatic dependent launch, so its launch overlaps
+//                        the row kernel and griddepcontrol.wait orders it.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -144,6 +146,9 @@ constexpr int APPEND_NT = 256;
 constexpr int APPEND_U = 8;
 
 __global__ void __launch_bounds__(APPEND_NT, 8) step_rows_kernel(const StepArgs a) {
+  // let the compaction kernel (a programmatic dependent launch) be scheduled
+  // now; it still waits for this whole grid before reading events
+  asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x;
   if (threadIdx.x == 0) {
     GuardRow r;
@@ -192,6 +197,9 @@ constexpr int COMPACT_NT = 1024;
 constexpr int COMPACT_RPT = 4;
 
 __global__ void __launch_bounds__(COMPACT_NT) step_compact_kernel(const StepArgs a) {
+  // launched as a programmatic dependent of step_rows_kernel: wait until that
+  // grid has completed and its writes (events) are visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ int warp_tot[COMPACT_NT / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int base = 0;
