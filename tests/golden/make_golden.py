@@ -26,6 +26,7 @@ Cases (inputs are seeded synthetic tensors; outputs come from the reference):
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 import types
 from pathlib import Path
@@ -275,8 +276,11 @@ def save(name, d):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("Q3S_REFERENCE"),
+                    help="reference checkout (default: $Q3S_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <reference checkout> or set Q3S_REFERENCE")
     ref_paths(Path(args.reference))
     torch.set_num_threads(1)
     save("gumbel_cb0_f32", case_gumbel(11, 8, bf16=False))

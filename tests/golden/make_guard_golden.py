@@ -23,12 +23,13 @@ Needs the reference tree (read-only) and runs in this container only; the GPU
 box uses the committed .npz.  Modules the engine imports but this path never
 calls (soxr, wetext, pypinyin) are stubbed as empty modules.
 
-    python tests/golden/make_guard_golden.py [reference_root]
+    python tests/golden/make_guard_golden.py <reference checkout>   (or Q3S_REFERENCE=...)
 """
 from __future__ import annotations
 
 import asyncio
 import logging
+import os
 import queue
 import sys
 import types
@@ -206,7 +207,10 @@ def run_scenario(ref, scen, seed):
 
 
 def main():
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("Q3S_REFERENCE")
+    if not arg:
+        sys.exit("usage: make_guard_golden.py <reference checkout> (or set Q3S_REFERENCE)")
+    root = Path(arg)
     ref = _import_reference(root)
     out = {"scenarios": np.array(SCENARIOS, np.float64), "eos_id": np.int64(EOS_ID)}
     for i, scen in enumerate(SCENARIOS):
