@@ -27,8 +27,11 @@
  *     scalar *_default field.
  *   - Calls are asynchronous on `stream` (a cudaStream_t passed as void*;
  *     NULL = the legacy default stream), never allocate, never synchronise,
- *     and are re-entrant: the library keeps no mutable state except a
- *     per-device SM-count cache and a thread-local error string.
+ *     and are re-entrant.  The library's only mutable state: per-device
+ *     caches of the SM count and of kernel attributes already set (atomics;
+ *     racing first calls store the same values), the process-wide kernel
+ *     policy of q3s_set_kernel_policy (an atomic int), and a thread-local
+ *     error string.
  *   - Arguments are validated on the host before any CUDA call; a bad
  *     argument returns Q3S_ERR_INVALID_ARGUMENT and launches nothing.
  *     q3s_last_error_string() explains the most recent failure of the
@@ -49,7 +52,7 @@
 extern "C" {
 #endif
 
-#define Q3S_ABI_VERSION 1
+#define Q3S_ABI_VERSION 2
 #define Q3S_MAX_VOCAB 8192     /* one CTA holds a whole row on chip */
 #define Q3S_MAX_TOPK 512       /* largest exactly-K candidate set (gumbel mode) */
 #define Q3S_MAX_CP_STAGES 64
@@ -84,6 +87,7 @@ typedef enum q3s_dtype { Q3S_DTYPE_F32 = 0, Q3S_DTYPE_BF16 = 1 } q3s_dtype;
 #define Q3S_DEVERR_NO_MASS 4           /* no finite logit survived (id = argmax) */
 #define Q3S_DEVERR_WAIT_TIMEOUT 8      /* a bounded device wait gave up */
 #define Q3S_DEVERR_CANDIDATES 16       /* exactly-K candidate set overflow */
+#define Q3S_DEVERR_HISTORY_FULL 32     /* capacity layout: a row's region is full (id not appended) */
 
 /* One sampling step over B rows (codebook 0, or one code-predictor stage). */
 typedef struct q3s_sample_desc {
@@ -102,7 +106,8 @@ typedef struct q3s_sample_desc {
   /* presence history: token_counts layout OR packed ragged layout (or none) */
   const int64_t* token_counts; /* [B, token_counts_row_stride] int64, count > 0 = appeared */
   int64_t token_counts_row_stride;
-  const int32_t* history;      /* packed ids; row b = history[offsets[b] .. offsets[b+1]) */
+  const int32_t* history;      /* packed ids; row b = history[offsets[b] .. offsets[b+1])
+                                  (capacity layout: see history_lengths at the end) */
   const int32_t* offsets;      /* [B+1] */
   int64_t history_len;         /* entries in `history` (bounds check) */
 
@@ -135,6 +140,12 @@ typedef struct q3s_sample_desc {
   int64_t processed_row_stride;
   int32_t* row_flags;          /* optional [B], Q3S_ROW_* bits */
   int32_t* error_word;         /* optional single device int32, Q3S_DEVERR_* bits */
+
+  /* capacity layout of the history (optional): row b's ids are
+   * history[offsets[b] .. offsets[b] + history_lengths[b]) inside its region
+   * [offsets[b], offsets[b+1]), so that q3s_step_update can append in place.
+   * NULL: the packed layout above. */
+  const int32_t* history_lengths; /* [B] */
 } q3s_sample_desc;
 
 /* Stage producer of the code-predictor frame. */
@@ -192,8 +203,9 @@ uint32_t q3s_desc_size(int32_t which);
  * then -log(-log(clamp(u, 1e-8, 1))) for the Gumbel noise).  One launch fills
  * out[i, 0..cols) for rows i = 0..rows-1 from Philox4x32-10 keyed by `seed`:
  * block j of row key r (row_keys[i], or row0 + i when row_keys is NULL) at
- * `step` uses counter (j, r mod 2^32, step, 0xA5A5); a 32-bit output x
- * becomes the uniform (x >> 8) * 2^-24 in [0, 1).  The same bits as the host
+ * `step` uses counter (j, r mod 2^32, step, 0xA5A5 ^ (r >> 32)) -- all 64
+ * bits of the key take part; below 2^32 the counter is (j, r, step, 0xA5A5)
+ * --; a 32-bit output x becomes the uniform (x >> 8) * 2^-24 in [0, 1).  The same bits as the host
  * generator q3s/philox.py (row_uniforms), so a row's numbers do not depend on
  * which batch or shard it sits in.  `out` and `row_keys` are device
  * pointers; asynchronous on `stream`. */
@@ -201,6 +213,19 @@ uint32_t q3s_desc_size(int32_t which);
 #define Q3S_PHILOX_GUMBEL 1    /* -log(-log(max(u, 1e-8))) in fp32 (gumbel_noise) */
 q3s_status q3s_philox_rows(uint64_t seed, uint32_t step, const int64_t* row_keys, int64_t row0, int32_t rows,
                            int32_t cols, int32_t kind, float* out, int64_t out_row_stride, void* stream);
+
+/* The same with one 64-bit seed per row as the Philox key: block j of row i
+ * at (step, stage) uses counter (j, step, stage, 0x5EED) under key
+ * (row_seeds[i] mod 2^32, row_seeds[i] >> 32).  This maps the reference's
+ * per-slot generators one to one: each slot's generator is seeded with the
+ * 63-bit blake2b digest of (base seed, request identity, segment[, retry])
+ * (_stable_sampling_seed, engine/backend/executor.py:79-86, used per slot at
+ * :3216-3254), so the host computes that seed once per segment (a retry gets
+ * its salted seed) and the device draws every step's numbers from it; `stage`
+ * separates the codebook-0 noise (e.g. 0) from the code-predictor stages.
+ * Host generator: q3s/philox.py seeded_uniforms. */
+q3s_status q3s_philox_seeds(const uint64_t* row_seeds, uint32_t step, uint32_t stage, int32_t rows, int32_t cols,
+                            int32_t kind, float* out, int64_t out_row_stride, void* stream);
 
 /* Per-step codec-0 epilogue on the device: EOS, frame counter, token loop
  * guard, packed history append.  The reference reads every row's codebook-0
@@ -264,9 +289,20 @@ typedef struct q3s_step_desc {
   int32_t* event_list;         /* [B] (row << 8) | bits for rows with any bit, ascending row */
   int32_t* event_count;        /* one int32: entries written to event_list (required with it) */
   int32_t* error_word;         /* Q3S_DEVERR_OFFSETS on bad offsets / capacity (row skipped) */
+
+  /* in-place append into the capacity layout (optional; then history_out
+   * must equal history and offsets_out is not used): row b's region is
+   * [offsets[b], offsets[b+1]) of history_out, its ids the first
+   * history_lengths[b] entries; ids[b] goes to history_out[offsets[b] +
+   * history_lengths[b]] and the length grows by one.  A full region gets
+   * nothing appended and sets Q3S_DEVERR_HISTORY_FULL.  O(B) bytes a step
+   * instead of the packed copy's O(sum of lengths). */
+  int32_t* history_lengths;    /* [B], read and updated */
 } q3s_step_desc;
 
-/* One epilogue step over B rows; asynchronous on `stream`, no allocation. */
+/* One epilogue step over B rows; asynchronous on `stream`, no allocation.
+ * Without the packed copy (history_out NULL, or the capacity layout's
+ * in-place append) one thread runs each row. */
 q3s_status q3s_step_update(const q3s_step_desc* desc, void* stream);
 
 /* Kernel family for icdf steps that either family can serve (process-wide;

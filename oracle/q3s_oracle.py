@@ -62,13 +62,27 @@ def suppress_mask(vocab_size: int = 3072, eos_id: int = 2150) -> np.ndarray:
     return m
 
 
-def appeared_from_packed(history: np.ndarray, offsets: np.ndarray, vocab: int) -> np.ndarray:
-    """Presence matrix bool[B,V] from a packed ragged history.  Ids outside
-    [0,V) are ignored (the kernel flags them in its error word)."""
-    B = len(offsets) - 1
+def row_spans(offsets: np.ndarray, lengths: np.ndarray | None = None) -> list[tuple[int, int]]:
+    """[start, end) of every row: offsets[b]..offsets[b+1] (packed), or the
+    first lengths[b] entries of the region offsets[b]..offsets[b+1]
+    (capacity layout)."""
+    o = np.asarray(offsets, np.int64)
+    if lengths is None:
+        return [(int(o[b]), int(o[b + 1])) for b in range(len(o) - 1)]
+    n = np.asarray(lengths, np.int64)
+    return [(int(o[b]), int(o[b] + n[b])) for b in range(len(o) - 1)]
+
+
+def appeared_from_packed(history: np.ndarray, offsets: np.ndarray, vocab: int,
+                         lengths: np.ndarray | None = None) -> np.ndarray:
+    """Presence matrix bool[B,V] from a packed ragged history (or its
+    capacity layout, ``lengths`` given).  Ids outside [0,V) are ignored (the
+    kernel flags them in its error word)."""
+    spans = row_spans(offsets, lengths)
+    B = len(spans)
     out = np.zeros((B, vocab), dtype=bool)
-    for b in range(B):
-        ids = np.asarray(history[offsets[b]:offsets[b + 1]], dtype=np.int64)
+    for b, (s0, s1) in enumerate(spans):
+        ids = np.asarray(history[s0:s1], dtype=np.int64)
         ids = ids[(ids >= 0) & (ids < vocab)]
         out[b, ids] = True
     return out
@@ -280,7 +294,7 @@ def inverse_cdf_draw(s: np.ndarray, u: np.ndarray):
 
 
 def sample_icdf(logits, *, uniforms, temperature=None, top_k=None, top_p=None, penalty=None,
-                history=None, offsets=None, token_counts=None,
+                history=None, offsets=None, token_counts=None, history_lengths=None,
                 suppress: np.ndarray | None = None, eos_id: int | None = None,
                 min_new_tokens=None, cur_len=None,
                 temperature_default=1.0, top_k_default=0, top_p_default=1.0,
@@ -300,13 +314,16 @@ def sample_icdf(logits, *, uniforms, temperature=None, top_k=None, top_p=None, p
     pen = _row_param(penalty, B, penalty_default, torch.float32)
     mn = _row_param(min_new_tokens, B, min_new_default, torch.int64)
     if cur_len is None:
-        cur_len = np.diff(np.asarray(offsets)) if offsets is not None else np.zeros(B, np.int64)
+        if history_lengths is not None:
+            cur_len = np.asarray(history_lengths, np.int64)
+        else:
+            cur_len = np.diff(np.asarray(offsets)) if offsets is not None else np.zeros(B, np.int64)
     cl = _row_param(cur_len, B, 0, torch.int64)
     appeared = None
     if token_counts is not None:
         appeared = torch.as_tensor(np.asarray(token_counts)) > 0
     elif history is not None:
-        appeared = torch.as_tensor(appeared_from_packed(history, offsets, V))
+        appeared = torch.as_tensor(appeared_from_packed(history, offsets, V, history_lengths))
     x = _apply_suppress_penalty(s, appeared, pen, suppress)
     x = _apply_eos_gate(x, eos_id, mn, cl)
 
@@ -393,7 +410,7 @@ def guard_thresholds(suspect: int, abort: int, emergency: int) -> tuple[int, int
 
 def step_update(ids, *, eos_id: int, state: dict, suspect: int = 0, abort: int = 0, emergency: int = 0,
                 min_ratio: float = 0.0, decode_start_frame=None, text_tokens=None, input_complete=None,
-                history=None, offsets=None):
+                history=None, offsets=None, history_lengths=None):
     """One step of the per-row codec-0 epilogue, row by row.
 
     * EOS: ``id == eos_id`` (engine/backend/executor.py:532-546); an EOS row
@@ -409,7 +426,12 @@ def step_update(ids, *, eos_id: int, state: dict, suspect: int = 0, abort: int =
     * history append: row b of the packed history gains ``ids[b]`` (the packed
       counterpart of ``token_counts + one_hot(id)``,
       scripts/export/talker_unified_modules.py:421-422, applied to every row);
-      ``offsets_out[b] = offsets[b] + b``.
+      ``offsets_out[b] = offsets[b] + b``.  With ``history_lengths`` (the
+      capacity layout: row b is the first lengths[b] entries of its region
+      offsets[b]..offsets[b+1]) the id goes in place after the row's last
+      one and the length grows by one; a full region gets nothing (the
+      kernel reports Q3S_DEVERR_HISTORY_FULL).  Then history_out is the
+      updated copy of ``history`` and offsets_out the updated lengths.
 
     ``state`` maps GUARD_FIELDS to int arrays [B], updated in place.  Returns
     (events [B] int32, run [B] int32 -- the ended run on RECOVERED, the run on
@@ -462,6 +484,15 @@ def step_update(ids, *, eos_id: int, state: dict, suspect: int = 0, abort: int =
             runs[b] = run
         events[b] = bits
     hist_out = off_out = None
+    if history is not None and history_lengths is not None:
+        hist_out = np.array(history, np.int32, copy=True)
+        o = np.asarray(offsets, np.int64)
+        off_out = np.array(history_lengths, np.int32, copy=True)
+        for b in range(B):
+            if o[b] + off_out[b] < o[b + 1]:
+                hist_out[o[b] + off_out[b]] = ids[b]
+                off_out[b] += 1
+        return events, runs, hist_out, off_out
     if history is not None:
         history = np.asarray(history, np.int32)
         offsets = np.asarray(offsets, np.int64)

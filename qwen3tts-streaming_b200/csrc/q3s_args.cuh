@@ -17,6 +17,7 @@ struct SampleArgs {
   const int32_t* history;
   const int32_t* offsets;
   int64_t history_len;
+  const int32_t* history_lengths;  // capacity layout: row b = [offsets[b], offsets[b] + len) inside its region
   const float* temperature;
   float temperature_default;
   const int32_t* top_k;

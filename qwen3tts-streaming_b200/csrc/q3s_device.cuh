@@ -120,6 +120,14 @@ Q3S_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------
+// Capacity layout: the end of a row of `len` ids starting at `start` inside
+// its region [start, region_end); -1 (an invalid end, flagged by the caller's
+// offsets check) when len is negative or passes the region.
+__device__ __forceinline__ int row_end_in_region(int start, int region_end, int len) {
+  const long long e = static_cast<long long>(start) + len;
+  return (len < 0 || e > region_end) ? -1 : static_cast<int>(e);
+}
+
 // per-CTA shared scratch
 // ---------------------------------------------------------------------------
 

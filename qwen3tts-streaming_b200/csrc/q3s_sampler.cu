@@ -20,6 +20,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -817,10 +818,11 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
   float x[E];
   uint32_t vmask;
   load_logits<BF16, E>(a.logits, static_cast<int64_t>(b) * a.row_stride, V, v0, shift, a.vec_logits, x, vmask);
-  int o0 = 0, o1 = 0;
+  int o0 = 0, o1 = 0, olen = -1;
   if (a.history) {
     o0 = __ldg(a.offsets + b);
-    o1 = __ldg(a.offsets + b + 1);
+    o1 = __ldg(a.offsets + b + 1);  // the row's end, or (capacity layout) its region's end
+    if (a.history_lengths) olen = __ldg(a.history_lengths + b);
   }
   uint32_t app = 0;
   if (a.token_counts) {
@@ -865,6 +867,7 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
 
   int hist_len = 0;
   if (a.history) {
+    if (a.history_lengths) o1 = row_end_in_region(o0, o1, olen);
     if (o0 < 0 || o1 < o0 || static_cast<int64_t>(o1) > a.history_len) {
       err |= Q3S_DEVERR_OFFSETS;
       o0 = o1 = 0;
@@ -1124,15 +1127,16 @@ q3s_status launch_rows(const q3s::SampleArgs& a, bool bf16, cudaStream_t st) {
 int g_policy = Q3S_POLICY_AUTO;
 
 int device_sm_count() {
-  static int cache[64] = {0};
+  // per-device cache; racing first readers store the same value
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 template <int NT, int E, bool BF16, int MODE>
@@ -1142,14 +1146,21 @@ q3s_status launch_cp_t(const q3s::CpArgs& a, cudaStream_t st) {
   if (dyn > 0) {
     // static + dynamic shared memory may pass the 48 KB default: opt in.
     // Idempotent per (kernel, device); the value only ever grows.
-    static int granted[64] = {0};
+    static std::atomic<int> granted[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || granted[dev] < static_cast<int>(dyn)) {
+    const bool known = dev >= 0 && dev < 64;
+    if (!known || granted[dev].load(std::memory_order_acquire) < static_cast<int>(dyn)) {
       const cudaError_t e =
           cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
       if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample_cp_frame smem attribute: %s", cudaGetErrorString(e));
-      if (dev >= 0 && dev < 64) granted[dev] = static_cast<int>(dyn);
+      if (known) {
+        // keep the largest grant: a racing smaller one must not lower it
+        int cur = granted[dev].load(std::memory_order_relaxed);
+        while (cur < static_cast<int>(dyn) &&
+               !granted[dev].compare_exchange_weak(cur, static_cast<int>(dyn), std::memory_order_release)) {
+        }
+      }
     }
   }
   int per_sm = 0;
@@ -1203,6 +1214,27 @@ q3s_status q3s_philox_rows(uint64_t seed, uint32_t step, const int64_t* row_keys
   return ok();
 }
 
+q3s_status q3s_philox_seeds(const uint64_t* row_seeds, uint32_t step, uint32_t stage, int32_t rows, int32_t cols,
+                            int32_t kind, float* out, int64_t out_row_stride, void* stream) {
+  if (rows < 0 || cols < 0) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_seeds: rows=%d cols=%d", rows, cols);
+  if (kind != Q3S_PHILOX_UNIFORM && kind != Q3S_PHILOX_GUMBEL)
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_seeds: unknown kind %d", kind);
+  if (rows == 0 || cols == 0) return ok();
+  if (!out || !row_seeds) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_seeds: out / row_seeds is NULL");
+  if (out_row_stride < cols)
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_seeds: out_row_stride %lld < cols %d",
+                static_cast<long long>(out_row_stride), cols);
+  const int64_t threads = static_cast<int64_t>(rows) * ((cols + 3) / 4);
+  const int nt = 256;
+  const int64_t grid = (threads + nt - 1) / nt;
+  if (grid > 0x7fffffffLL) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_philox_seeds: too many rows x columns");
+  q3s::philox_seeds_kernel<<<static_cast<unsigned>(grid), nt, 0, static_cast<cudaStream_t>(stream)>>>(
+      row_seeds, step, stage, rows, cols, kind, out, out_row_stride);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_philox_seeds launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
+
 uint32_t q3s_desc_size(int32_t which) {
   if (which == 0) return static_cast<uint32_t>(sizeof(q3s_sample_desc));
   if (which == 1) return static_cast<uint32_t>(sizeof(q3s_cp_frame_desc));
@@ -1245,7 +1277,17 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: event_list needs event_count");
   if (d->event_count && !d->events)
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: event_list / event_count are compacted from events");
-  const bool append = d->history_out != nullptr;
+  const bool in_place = d->history_lengths != nullptr;
+  const bool append = d->history_out != nullptr && !in_place;
+  if (in_place) {
+    if (!d->history_out || static_cast<const void*>(d->history_out) != static_cast<const void*>(d->history) ||
+        !d->offsets)
+      return fail(Q3S_ERR_INVALID_ARGUMENT,
+                  "q3s_step_update: the in-place append (history_lengths) needs offsets and history_out == history");
+    if (d->history_out_capacity < 0 || d->history_out_capacity > INT32_MAX)
+      return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_step_update: history_out_capacity %lld outside [0, 2^31)",
+                  static_cast<long long>(d->history_out_capacity));
+  }
   if (append) {
     if ((!d->history && d->history_len > 0) || !d->offsets || !d->offsets_out)
       return fail(Q3S_ERR_INVALID_ARGUMENT,
@@ -1283,8 +1325,12 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
   a.event_list = d->event_list;
   a.event_count = d->event_count;
   a.error_word = d->error_word;
+  a.history_lengths = d->history_lengths;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  q3s::step_rows_kernel<<<static_cast<unsigned>(B), append ? q3s::APPEND_NT : 32, 0, st>>>(a);
+  if (append)
+    q3s::step_rows_kernel<<<static_cast<unsigned>(B), q3s::APPEND_NT, 0, st>>>(a);
+  else
+    q3s::step_lite_kernel<<<static_cast<unsigned>((B + q3s::LITE_NT - 1) / q3s::LITE_NT), q3s::LITE_NT, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && (d->event_list || d->event_count)) {
     cudaLaunchConfig_t lc = {};
@@ -1329,6 +1375,8 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample: token_counts_row_stride < vocab");
   if (d->history && (!d->offsets || d->history_len < 0))
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample: packed history needs offsets and history_len >= 0");
+  if (d->history_lengths && !d->history)
+    return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample: history_lengths (capacity layout) needs history and offsets");
   if (d->counts_out && !d->token_counts)
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample: counts_out needs token_counts");
   if (d->counts_out && d->counts_out_row_stride < V)
@@ -1367,6 +1415,7 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
   a.history = d->history;
   a.offsets = d->offsets;
   a.history_len = d->history_len;
+  a.history_lengths = d->history_lengths;
   a.temperature = d->temperature;
   a.temperature_default = d->temperature_default;
   a.top_k = d->top_k;
@@ -1396,7 +1445,7 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
   a.vec_history = d->history && aligned16(d->history);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool warp_ok = a.mode == Q3S_DRAW_ICDF && !a.token_counts && !a.col_shift && !a.processed &&
+  const bool warp_ok = a.mode == Q3S_DRAW_ICDF && !a.token_counts && !a.col_shift &&
                        !a.counts_out && V % 8 == 0 && V > 1024 && V <= 3072 && a.vec_logits &&
                        (!a.suppress || a.vec_suppress);
   const int policy = __atomic_load_n(&g_policy, __ATOMIC_RELAXED);

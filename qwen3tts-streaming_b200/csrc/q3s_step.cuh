@@ -12,7 +12,10 @@
 //                                         scripts/export/talker_unified_modules.py:421-422
 //
 // Two launches on the caller's stream:
-//   step_rows_kernel     CTA b: thread 0 runs row b's guard (events[b],
+//   step_lite_kernel     one thread per row: the guard, and with the capacity
+//                        layout the in-place append (history[offsets[b] +
+//                        len[b]] = ids[b], len[b] += 1): O(B) bytes a step;
+//   step_rows_kernel     (packed layout, copied append) CTA b: thread 0 runs row b's guard (events[b],
 //                        event_run[b], state) while the CTA copies history row
 //                        b to its shifted place in the output
 //                        (offsets_out[b] = offsets[b] + b) and appends ids[b];
@@ -58,6 +61,7 @@ struct StepArgs {
   int32_t* event_list;
   int32_t* event_count;
   int32_t* error_word;
+  int32_t* history_lengths;       // capacity layout: in-place append into history_out
 };
 
 __device__ __forceinline__ int64_t step_id(const StepArgs& a, int b) {
@@ -187,6 +191,35 @@ __global__ void __launch_bounds__(APPEND_NT, 8) step_rows_kernel(const StepArgs 
     }
   }
   if (threadIdx.x == 0) dst[n] = static_cast<int32_t>(step_id(a, b));
+}
+
+// One thread per row: the guard, and with the capacity layout the in-place
+// append of ids[b] at the end of row b inside its region [offsets[b],
+// offsets[b+1]) of history_out.  A full region gets nothing (and
+// Q3S_DEVERR_HISTORY_FULL), an inconsistent one Q3S_DEVERR_OFFSETS.
+constexpr int LITE_NT = 128;
+
+__global__ void __launch_bounds__(LITE_NT) step_lite_kernel(const StepArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int b = static_cast<int>(blockIdx.x) * LITE_NT + static_cast<int>(threadIdx.x);
+  if (b >= a.batch) return;
+  GuardRow r;
+  guard_load(a, b, r);
+  int ev_run;
+  const int bits = guard_apply(a, b, r, ev_run);
+  if (a.events) a.events[b] = bits;
+  if (a.event_run) a.event_run[b] = ev_run;
+  if (!a.history_lengths) return;
+  const int64_t s = a.offsets[b], e = a.offsets[b + 1];
+  const int len = a.history_lengths[b];
+  if (s < 0 || e < s || e > a.history_out_capacity || len < 0 || s + len > e) {
+    if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_OFFSETS);
+  } else if (s + len == e) {
+    if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_HISTORY_FULL);
+  } else {
+    a.history_out[s + len] = static_cast<int32_t>(r.id);
+    a.history_lengths[b] = len + 1;
+  }
 }
 
 // Ordered compaction of events[0, B) into event_list ((row << 8) | bits for

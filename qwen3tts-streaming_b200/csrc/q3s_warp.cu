@@ -3,6 +3,9 @@
 // q3s_sampler.cu.
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
+
 #include "q3s_args.cuh"
 #include "q3s_warp.cuh"
 
@@ -12,17 +15,24 @@ namespace {
 template <int R, int W>
 cudaError_t launch_smem(const SampleArgs& a, bool bf16, cudaStream_t st) {
   const size_t dyn = row_smem_bytes<R, W>(bf16);
-  auto kern = bf16 ? sample_smem_kernel<R, W, true> : sample_smem_kernel<R, W, false>;
-  // the largest shared-memory carveout, so that ~11 rows fit per SM; set once
-  // per (kernel, device)
-  static bool done[2][64] = {{false}};
+  const bool proc = a.processed != nullptr;
+  const int v = (bf16 ? 2 : 0) + (proc ? 1 : 0);
+  using Kern = void (*)(const SampleArgs);
+  const Kern kerns[4] = {sample_smem_kernel<R, W, false, false>, sample_smem_kernel<R, W, false, true>,
+                         sample_smem_kernel<R, W, true, false>, sample_smem_kernel<R, W, true, true>};
+  const Kern kern = kerns[v];
+  // the shared-memory opt-in and the largest carveout (so that ~11 rows fit
+  // per SM), set once per (variant, device): one bit per device; two threads
+  // racing on a first launch both set the same attributes, which is harmless
+  static std::atomic<uint64_t> done[4];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !done[bf16 ? 1 : 0][dev]) {
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (!bit || !(done[v].load(std::memory_order_acquire) & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) done[bf16 ? 1 : 0][dev] = true;
+    done[v].fetch_or(bit, std::memory_order_release);
   }
   kern<<<a.B, W * 32, dyn, st>>>(a);
   return cudaGetLastError();

@@ -740,7 +740,10 @@ constexpr int row_min_blocks(int W, bool bf16) {
   return W >= 12 ? 2 : W == 8 ? 4 : W == 4 ? (bf16 ? 8 : 7) : W == 2 ? 14 : 17;
 }
 
-template <int R, int W, bool BF16>
+// PROC adds the verification-only processed-logits output (the row as HF's
+// processors hand it to the draw: x'/T with the entries top-k and top-p
+// remove at -inf; greedy rows x'); the timed variants carry none of it.
+template <int R, int W, bool BF16, bool PROC>
 __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_kernel(const SampleArgs a) {
   extern __shared__ __align__(16) unsigned char q3s_row_smem[];
   using Smem = RowSmem<R, W>;
@@ -768,10 +771,11 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
 
   // ---- first loads: offsets and the suppress words of this warp's quads
   //      (L2-resident: every row reads them) ---------------------------------
-  int o0 = 0, o1 = 0;
+  int o0 = 0, o1 = 0, olen = -1;
   if (history) {
     o0 = __ldg(a.offsets + b);
-    o1 = __ldg(a.offsets + b + 1);
+    o1 = __ldg(a.offsets + b + 1);  // the row's end, or (capacity layout) its region's end
+    if (a.history_lengths) olen = __ldg(a.history_lengths + b);
   }
   const float T = a.temperature ? __ldg(a.temperature + b) : a.temperature_default;
   const float pen = a.penalty ? __ldg(a.penalty + b) : a.penalty_default;
@@ -810,6 +814,7 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
   // set); racing stores of the same byte need no atomics
   int hist_len = 0;
   if (history) {
+    if (a.history_lengths) o1 = row_end_in_region(o0, o1, olen);
     if (o0 < 0 || o1 < o0 || static_cast<int64_t>(o1) > a.history_len) {
       err |= Q3S_DEVERR_OFFSETS;
       o0 = o1 = 0;
@@ -859,6 +864,10 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
   const bool gate = eos_id >= 0 && eos_id < V && cur < min_new;
 
   int id = 0, flags = 0;
+  // how the row was finished (read by the processed-logits output only)
+  bool list_row = false;             // by the candidate list (non-greedy)
+  bool wv_topk = false, wv_cut = false, wv_single = false, wv_nomass = false;
+  uint32_t wv_kth = 0;
   const bool greedy = !(T > 0.0f);
   const int K = greedy ? 1 : kk;
   const bool few = greedy || (kk > 0 && kk < V);
@@ -1149,6 +1158,9 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
       //      the proof window -- one exchange -------------------------------
       float* sf = rowf;
       float m = -INFINITY, bad = 0.0f;
+      // the K-th largest s (slot n - K below); with fewer than K candidates
+      // every one is kept
+      if (t == 0) *reinterpret_cast<float*>(&sh.sel[0]) = -INFINITY;
       for (int p = t; p < n4; p += NT) {
         if (p < n) {
           const uint32_t v = sh.u.cand[p].y;
@@ -1291,6 +1303,9 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
             }
             const int icut = min(8 * lc + __shfl_sync(FULL, below, lc), n - 1);
             if (__shfl_sync(FULL, near, lc)) lflags |= Q3S_ROW_TOPP_BOUNDARY;
+            if constexpr (PROC) {
+              if (lane == 0) sh.res[2] = icut;
+            }
             int sa[WCAP / 32];
 #pragma unroll
             for (int r = 0; r < WCAP / 32; ++r) sa[r] = r < P && lane * P + r < n ? asca[lane * P + r] : WCAP;
@@ -1299,11 +1314,18 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
               if (sa[r] < icut) wk[lane * P + r] = 0.0f;
             __syncwarp();
           }
+          if constexpr (PROC) {
+            if (!cut && lane == 0) sh.res[2] = 0;
+          }
           const int pos = warp_draw_list(wk, n, u, lflags);
           id = static_cast<int>(sh.u.cand[pos].y);
           flags = lflags;
         }
         done = true;
+        list_row = true;
+        if constexpr (PROC) {
+          if (t == 0) sh.lcnt[0] = n;
+        }
       }
     }
     if (!done) {
@@ -1343,6 +1365,7 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
       const float m = X.max_f(lm);
       if (m == -INFINITY) {
         // nothing finite: report it and take the lowest index
+        wv_nomass = true;
         err |= Q3S_DEVERR_NO_MASS;
         flags = Q3S_ROW_FALLBACK;
         id = 0;
@@ -1370,6 +1393,9 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
         //      coarse histogram by the weight's exponent and top 4 mantissa
         //      bits (monotone in s) ------------------------------------------
         const bool cut = top_p < 1.0f;
+        wv_topk = topk;
+        wv_kth = kth;
+        wv_cut = cut;
         constexpr uint32_t LO = (1u << MASS_LO_BITS) - 1u;
         // one loop per (top-k, top-p) combination, picked once per row
         auto weights_pass = [&](auto topk_tag, auto cut_tag) {
@@ -1439,6 +1465,7 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
             }
             id = X.max_i(last);
             single = true;
+            wv_single = true;
           } else {
             // entries below the crossing bin go (their weights are zeroed),
             // entries above it stay; the crossing bin's entries are resolved
@@ -1721,6 +1748,49 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
             flags |= sh.res[1];
           }
         }
+      }
+    }
+  }
+  if constexpr (PROC) {
+    // Verification output, written after the row is decided: every entry's
+    // exact processed value where top-k and top-p keep it, -inf elsewhere
+    // (greedy rows: x' everywhere, the input of torch.argmax).  List rows
+    // write -inf for all entries, then (after a barrier) the kept candidates.
+    row_sync<W>();
+    float* const prow = a.processed + static_cast<int64_t>(b) * a.proc_stride;
+#pragma unroll 1
+    for (int r = rb0; r < rb1; ++r) {
+      const int h = lane + 32 * r;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int v = 4 * h + j;
+        if (v >= V) continue;
+        float o;
+        if (greedy) {
+          o = exact_x(v);
+        } else if (list_row) {
+          o = -INFINITY;
+        } else {
+          const float s = exact_s(v);
+          bool kept;
+          if (wv_nomass) kept = true;
+          else if (wv_single) kept = v == id;
+          else if (wv_cut) kept = rowf[v] > 0.0f;
+          else kept = !wv_topk || f2key(s) >= wv_kth;
+          o = kept ? s : -INFINITY;
+        }
+        prow[v] = o;
+      }
+    }
+    if (list_row) {
+      row_sync<W>();
+      const float sK = *reinterpret_cast<const float*>(&sh.sel[0]);
+      const int icut = sh.res[2], n = sh.lcnt[0];
+      const uint8_t* asca = sh.cmask;
+      for (int p = t; p < n; p += NT) {
+        const uint4 c = sh.u.cand[p];
+        const float s = __uint_as_float(c.x);
+        if (s >= sK && static_cast<int>(asca[p]) >= icut) prow[c.y] = s;
       }
     }
   }

@@ -13,7 +13,7 @@ from pathlib import Path
 
 from .build import LIB_PATH
 
-Q3S_ABI_VERSION = 1
+Q3S_ABI_VERSION = 2
 MAX_VOCAB = 8192
 MAX_TOPK = 512
 MAX_CP_STAGES = 64
@@ -28,6 +28,7 @@ PHILOX_UNIFORM, PHILOX_GUMBEL = 0, 1
 
 ROW_DRAW_BOUNDARY, ROW_TOPP_BOUNDARY, ROW_GREEDY, ROW_FALLBACK = 1, 2, 4, 8
 DEVERR_HISTORY_ID, DEVERR_OFFSETS, DEVERR_NO_MASS, DEVERR_WAIT_TIMEOUT, DEVERR_CANDIDATES = 1, 2, 4, 8, 16
+DEVERR_HISTORY_FULL = 32
 
 _p = C.c_void_p
 
@@ -72,6 +73,7 @@ class SampleDesc(C.Structure):
         ("processed_row_stride", C.c_int64),
         ("row_flags", _p),
         ("error_word", _p),
+        ("history_lengths", _p),
     ]
 
 
@@ -139,6 +141,7 @@ class StepDesc(C.Structure):
         ("event_list", _p),
         ("event_count", _p),
         ("error_word", _p),
+        ("history_lengths", _p),
     ]
 
 
@@ -151,6 +154,7 @@ EXPORTS = (
     "q3s_desc_size",
     "q3s_set_kernel_policy",
     "q3s_philox_rows",
+    "q3s_philox_seeds",
     "q3s_step_update",
 )
 
@@ -185,6 +189,9 @@ def load(path: str | Path | None = None) -> C.CDLL:
         lib.q3s_philox_rows.argtypes = [C.c_uint64, C.c_uint32, _p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                         _p, C.c_int64, _p]
         lib.q3s_philox_rows.restype = C.c_int
+        lib.q3s_philox_seeds.argtypes = [_p, C.c_uint32, C.c_uint32, C.c_int32, C.c_int32, C.c_int32, _p, C.c_int64,
+                                         _p]
+        lib.q3s_philox_seeds.restype = C.c_int
         lib.q3s_step_update.argtypes = [C.POINTER(StepDesc), _p]
         lib.q3s_step_update.restype = C.c_int
         if lib.q3s_abi_version() != Q3S_ABI_VERSION:

@@ -148,6 +148,35 @@ def philox_rows(seed: int, rows: int, cols: int, *, step: int = 0, row0: int = 0
     return out
 
 
+def philox_seeds(row_seeds: torch.Tensor, cols: int, *, step: int = 0, stage: int = 0, kind: str = "uniform",
+                 out: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Per-row randomness from one 64-bit seed per row (``row_seeds``: int64
+    [B] on the device, read as unsigned) in one launch: fp32 ``[B, cols]``
+    uniforms or Gumbel noise, the same bits as
+    ``q3s.philox.seeded_uniforms(seeds, cols, step, stage)``.  The row's seed
+    is its Philox key, so the reference's per-slot seeds
+    (engine/backend/executor.py:79-86, a retry's salted seed included) map
+    one to one; ``stage`` separates codebook 0 from the code-predictor
+    stages."""
+    lib = _lib.load()
+    if kind not in ("uniform", "gumbel"):
+        raise ValueError(f"kind must be 'uniform' or 'gumbel', got {kind!r}")
+    if row_seeds.device.type != "cuda":
+        raise RuntimeError("row_seeds must be a CUDA tensor (no CPU fallback)")
+    seeds = row_seeds.reshape(-1).to(torch.int64).contiguous()
+    rows = seeds.numel()
+    if out is None:
+        out = torch.empty(rows, cols, dtype=torch.float32, device=seeds.device)
+    elif out.dtype != torch.float32 or out.dim() != 2 or out.shape != (rows, cols) or out.stride(1) != 1:
+        raise ValueError("out must be fp32 [rows, cols] with unit column stride")
+    kcode = _lib.PHILOX_UNIFORM if kind == "uniform" else _lib.PHILOX_GUMBEL
+    _lib.check(lib.q3s_philox_seeds(seeds.data_ptr() if rows else None, int(step) & 0xFFFFFFFF,
+                                    int(stage) & 0xFFFFFFFF, rows, int(cols), kcode,
+                                    out.data_ptr() if out.numel() else None, out.stride(0) if out.numel() else cols,
+                                    _stream_handle(stream)), "q3s_philox_seeds")
+    return out
+
+
 def set_kernel_policy(policy: str) -> str:
     """Choose the kernel family for icdf steps (process-wide): "auto", "cta"
     (register-resident CTA per row), "warp" (shared-memory row kernel, warps
@@ -183,6 +212,7 @@ class SamplePlan:
     def __init__(self, logits: torch.Tensor, *, mode: str = "icdf", topk: int = DEFAULT_TOPK,
                  token_counts: Optional[torch.Tensor] = None,
                  history: Optional[torch.Tensor] = None, offsets: Optional[torch.Tensor] = None,
+                 history_lengths: Optional[torch.Tensor] = None,
                  temperature: TensorOrScalar = 1.0, top_k: Optional[torch.Tensor] = None,
                  top_p: TensorOrScalar = 1.0, penalty: TensorOrScalar = 1.0,
                  min_new_tokens: TensorOrScalar = 0, cur_len: Optional[torch.Tensor] = None,
@@ -238,6 +268,16 @@ class SamplePlan:
             d.history = history.data_ptr() if history.numel() else offsets.data_ptr()
             d.offsets = offsets.data_ptr()
             d.history_len = history.numel()
+            if history_lengths is not None:
+                # capacity layout: row b = history[offsets[b] : offsets[b] + history_lengths[b]]
+                _need_cuda(history_lengths, "history_lengths", dev)
+                if history_lengths.dtype != torch.int32 or history_lengths.numel() != B or \
+                        not history_lengths.is_contiguous():
+                    raise ValueError("history_lengths must be a contiguous int32 [B] tensor")
+                keep.append(history_lengths)
+                d.history_lengths = history_lengths.data_ptr()
+        elif history_lengths is not None:
+            raise ValueError("history_lengths needs history and offsets")
         t, tv = _row_param(temperature, B, torch.float32, dev, "temperature")
         d.temperature, d.temperature_default = _ptr(t), float(tv if t is None else 0.0)
         p, pv = _row_param(top_p, B, torch.float32, dev, "top_p")
@@ -406,6 +446,20 @@ class CpFramePlan:
 # reference-shaped functions
 # ---------------------------------------------------------------------------
 
+def _torch_ops():
+    from . import torch_ops
+
+    return torch_ops.load()
+
+
+def _as_rows(x: TensorOrScalar, device: torch.device) -> torch.Tensor:
+    """A per-row parameter as a tensor (a scalar as one value the operator
+    broadcasts to every row)."""
+    if isinstance(x, torch.Tensor):
+        return x
+    return torch.full((1,), float(1.0 if x is None else x), dtype=torch.float32, device=device)
+
+
 def sample_codebook0(logits: torch.Tensor, token_counts: torch.Tensor, gumbel_noise: torch.Tensor,
                      temperature: TensorOrScalar, penalty: TensorOrScalar, *,
                      suppress: Optional[torch.Tensor] = None, topk: int = DEFAULT_TOPK,
@@ -418,28 +472,27 @@ def sample_codebook0(logits: torch.Tensor, token_counts: torch.Tensor, gumbel_no
     ``temperature`` / ``penalty`` fp32 [B,1] (or scalars), ``suppress`` bool
     [V] (the module's ``suppress_mask`` buffer).  Returns ``codec_token_0``
     int64 [B] and ``updated_token_counts`` = token_counts + one_hot(id): a new
-    tensor, or ``token_counts`` itself updated when ``inplace``."""
-    logits = _rows_2d(logits)
-    counts_out = token_counts if inplace else torch.empty_like(token_counts)
-    plan = SamplePlan(logits, mode="gumbel", topk=topk, token_counts=token_counts,
-                      temperature=temperature, penalty=penalty, gumbel_noise=gumbel_noise,
-                      suppress_mask=suppress, counts_out=counts_out)
-    plan.launch()
-    return plan.ids, counts_out
+    tensor, or ``token_counts`` itself updated when ``inplace``.  Runs the
+    registered operator ``torch.ops.q3s.sample_codebook0`` (``_`` in place)."""
+    ops = _torch_ops()
+    dev = logits.device
+    T = _as_rows(temperature, dev)
+    P = _as_rows(penalty, dev)
+    if inplace:
+        return ops.sample_codebook0_(logits, token_counts, gumbel_noise, T, P, suppress, int(topk)), token_counts
+    return ops.sample_codebook0(logits, token_counts, gumbel_noise, T, P, suppress, int(topk))
 
 
 def select_token(logits: torch.Tensor, *, temperature: TensorOrScalar = None,
                  gumbel_noise: Optional[torch.Tensor] = None, topk: int = DEFAULT_TOPK) -> torch.Tensor:
     """Drop-in for ``CodePredictorUnrolled._select_token`` (utils.py:1178-1193):
     ``logits`` [B,1,V] or [B,V]; no noise -> argmax over the full row; else
-    top-min(K,V) -> /T -> +noise -> argmax -> gather.  Returns int64 [B]."""
+    top-min(K,V) -> /T -> +noise -> argmax -> gather.  Returns int64 [B].
+    Runs the registered operator ``torch.ops.q3s.sample_cp_stage``."""
     if logits.dim() == 3:
         logits = logits.squeeze(1)
-    plan = SamplePlan(logits, mode="gumbel", topk=min(int(topk), logits.shape[-1]),
-                      temperature=1.0 if temperature is None else temperature,
-                      gumbel_noise=None if gumbel_noise is None else gumbel_noise.reshape(logits.shape[0], -1))
-    plan.launch()
-    return plan.ids
+    T = None if temperature is None else _as_rows(temperature, logits.device)
+    return _torch_ops().sample_cp_stage(logits, T, gumbel_noise, int(topk))
 
 
 def _packed_from_hist(hist: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

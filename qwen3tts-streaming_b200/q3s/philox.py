@@ -78,8 +78,9 @@ def row_uniforms(seed: int, rows: np.ndarray | int, cols: int = 1, step: int = 0
     per-lane independence the reference pins for its per-slot generators
     (tests/unit/engine_core/test_executor_trt_engine.py:250-267).
 
-    Returns fp32 ``[len(rows), cols]``; block j of row r uses counter
-    ``(j, r, step, 0xA5A5)`` under key ``seed``."""
+    Returns fp32 ``[len(rows), cols]``; block j of row key r (any 64-bit
+    value) uses counter ``(j, r mod 2^32, step, 0xA5A5 ^ (r >> 32))`` under
+    key ``seed`` -- for r < 2^32 that is ``(j, r, step, 0xA5A5)``."""
     r = np.arange(rows) if np.isscalar(rows) else np.asarray(rows)
     r = r.astype(np.uint64)
     nblk = (int(cols) + 3) // 4
@@ -87,10 +88,31 @@ def row_uniforms(seed: int, rows: np.ndarray | int, cols: int = 1, step: int = 0
     ctr[:, :, 0] = np.arange(nblk, dtype=np.uint32)[None, :]
     ctr[:, :, 1] = (r & np.uint64(0xFFFFFFFF)).astype(np.uint32)[:, None]
     ctr[:, :, 2] = np.uint32(int(step) & 0xFFFFFFFF)
-    ctr[:, :, 3] = np.uint32(0xA5A5)
+    ctr[:, :, 3] = (np.uint64(0xA5A5) ^ (r >> np.uint64(32))).astype(np.uint32)[:, None]
     seed = int(seed) & 0xFFFFFFFFFFFFFFFF
     key = np.array([seed & 0xFFFFFFFF, seed >> 32], dtype=np.uint32)
     bits = philox4x32_10(ctr, key).reshape(r.shape[0], nblk * 4)[:, :cols]
+    return uint32_to_unit_float(bits)
+
+
+def seeded_uniforms(seeds, cols: int, step: int = 0, stage: int = 0) -> np.ndarray:
+    """Per-row uniforms from one 64-bit seed per row (the row's Philox key):
+    block j of a row with seed q at (step, stage) uses counter
+    ``(j, step, stage, 0x5EED)`` under key ``(q mod 2^32, q >> 32)``.  The
+    reference seeds one generator per slot with a 63-bit blake2b digest of
+    (base seed, request identity, segment[, retry])
+    (engine/backend/executor.py:79-86, 3216-3254); with that digest as the
+    row's seed, a slot's numbers are its seed's alone, whatever batch or
+    shard it sits in.  Returns fp32 ``[len(seeds), cols]``."""
+    q = np.asarray([int(x) & 0xFFFFFFFFFFFFFFFF for x in np.atleast_1d(seeds)], dtype=np.uint64)
+    nblk = (int(cols) + 3) // 4
+    ctr = np.zeros((q.shape[0], nblk, 4), dtype=np.uint32)
+    ctr[:, :, 0] = np.arange(nblk, dtype=np.uint32)[None, :]
+    ctr[:, :, 1] = np.uint32(int(step) & 0xFFFFFFFF)
+    ctr[:, :, 2] = np.uint32(int(stage) & 0xFFFFFFFF)
+    ctr[:, :, 3] = np.uint32(0x5EED)
+    key = np.stack([(q & np.uint64(0xFFFFFFFF)).astype(np.uint32), (q >> np.uint64(32)).astype(np.uint32)], -1)
+    bits = philox4x32_10(ctr, key[:, None, :]).reshape(q.shape[0], nblk * 4)[:, :cols]
     return uint32_to_unit_float(bits)
 
 

@@ -11,6 +11,12 @@ The per-step codec-0 epilogue of the reference -- EOS detection
 segment 0 of its own session, so an abort never takes the retry path (a retry
 needs an earlier live segment, engine_loop.py:3443-3450) and ends the stream.
 
+The last scenarios (DYNAMIC) also change each stream's generation progress
+mid-run, as the reference does while a segment streams in
+(engine/backend/engine_loop.py:930-1000 raises text_tokens_consumed,
+:1027 sets input_complete): before step t the segment gets that step's text
+count and completion flag, recorded as s<i>_progress [STEPS, STREAMS, 2].
+
 Recorded per scenario, step t and stream s: whether s was active before the
 step, the codec-0 token fed, the events the reference emitted (read from its
 log records: "Loop suspect", "Loop recovered", "Loop deferred", "Loop
@@ -53,8 +59,30 @@ SCENARIOS = [
     (4, 0, 2.0, 20),    # guard off: only EOS and the frame counter
     (2, 7, 3.25, 0),    # progress gate, no emergency stage
 ]
+# scenarios whose text count and completion flag change between steps
+DYNAMIC = [
+    (4, 10, 2.0, 20),
+    (3, 6, 1.0, 0),
+    (2, 5, 0.5, 12),
+]
 STREAMS = 16
 STEPS = 64
+
+
+def _progress_schedule(rng: np.random.Generator, text0: int, complete0: bool):
+    """Per-step (text_tokens_consumed, input_complete) of one stream: text
+    arrives in bursts until the input completes at a random step (or was
+    complete from the start)."""
+    text = np.empty(STEPS, np.int64)
+    comp = np.empty(STEPS, np.int64)
+    t_done = 0 if complete0 else int(rng.integers(1, STEPS + 8))
+    cur = text0
+    for t in range(STEPS):
+        done = t >= t_done
+        if not done and rng.random() < 0.35:
+            cur += int(rng.integers(1, 4))
+        text[t], comp[t] = cur, int(done)
+    return text, comp
 
 
 def _import_reference(root: Path):
@@ -119,7 +147,7 @@ def _stream_inputs(rng: np.random.Generator):
     return frame0, start, text, complete, toks
 
 
-def run_scenario(ref, scen, seed):
+def run_scenario(ref, scen, seed, dynamic=False):
     EngineLoop, EngineSegment, StepOutput, KVCachePool, ModelConfig, EngineRequest, RequestType = ref
     import torch
 
@@ -143,6 +171,9 @@ def run_scenario(ref, scen, seed):
     segs, slots = [], []
     consts = np.zeros((STREAMS, 4), np.int64)  # frame0, decode_start_frame, text_tokens, input_complete
     tokens = np.zeros((STEPS, STREAMS), np.int64)
+    prng = np.random.default_rng(seed + 50000)  # progress schedules (dynamic scenarios only)
+    prog_text = np.zeros((STEPS, STREAMS), np.int64)
+    prog_comp = np.zeros((STEPS, STREAMS), np.int64)
     for s in range(STREAMS):
         sid = f"s{s}"
         el._handle_request(EngineRequest(type=RequestType.NEW_SESSION, session_id=sid, result_queue=queue.Queue()))
@@ -159,6 +190,8 @@ def run_scenario(ref, scen, seed):
         seg.input_complete = complete
         consts[s] = (frame0, start, text, int(complete))
         tokens[:, s] = toks
+        if dynamic:
+            prog_text[:, s], prog_comp[:, s] = _progress_schedule(prng, text, complete)
         segs.append(seg)
         slots.append(slot)
 
@@ -178,6 +211,10 @@ def run_scenario(ref, scen, seed):
             if not rows:
                 break
             handler.rows.clear()
+            if dynamic:
+                for s in rows:
+                    segs[s].text_tokens_consumed = int(prog_text[t, s])
+                    segs[s].input_complete = bool(prog_comp[t, s])
             out = StepOutput(slots=[slots[s] for s in rows],
                              eos_flags=[bool(tokens[t, s] == EOS_ID) for s in rows],
                              tokens=[int(tokens[t, s]) for s in rows], audio_chunks=[audio for _ in rows],
@@ -203,7 +240,10 @@ def run_scenario(ref, scen, seed):
         lg.removeHandler(handler)
         lg.setLevel(old_level)
         loop.close()
-    return dict(consts=consts, tokens=tokens, active=active, events=events, runs=runs, state=state)
+    r = dict(consts=consts, tokens=tokens, active=active, events=events, runs=runs, state=state)
+    if dynamic:
+        r["progress"] = np.stack([prog_text, prog_comp], axis=-1)
+    return r
 
 
 def main():
@@ -212,13 +252,16 @@ def main():
         sys.exit("usage: make_guard_golden.py <reference checkout> (or set Q3S_REFERENCE)")
     root = Path(arg)
     ref = _import_reference(root)
-    out = {"scenarios": np.array(SCENARIOS, np.float64), "eos_id": np.int64(EOS_ID)}
-    for i, scen in enumerate(SCENARIOS):
-        r = run_scenario(ref, scen, seed=7100 + i)
+    allscen = SCENARIOS + DYNAMIC
+    out = {"scenarios": np.array(allscen, np.float64), "eos_id": np.int64(EOS_ID),
+           "dynamic": np.array([0] * len(SCENARIOS) + [1] * len(DYNAMIC), np.int64)}
+    for i, scen in enumerate(allscen):
+        dyn = i >= len(SCENARIOS)
+        r = run_scenario(ref, scen, seed=(7100 + i) if not dyn else (7300 + i), dynamic=dyn)
         for k, v in r.items():
             out[f"s{i}_{k}"] = v
         ev = r["events"]
-        print(f"scenario {scen}: eos={int((ev & EVT_EOS).astype(bool).sum())} "
+        print(f"scenario {scen}{' (progress changes mid-run)' if dyn else ''}: eos={int((ev & EVT_EOS).astype(bool).sum())} "
               f"suspect={int((ev & EVT_SUSPECT).astype(bool).sum())} "
               f"recovered={int((ev & EVT_RECOVERED).astype(bool).sum())} "
               f"deferred={int((ev & EVT_DEFERRED).astype(bool).sum())} "

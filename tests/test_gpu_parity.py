@@ -373,25 +373,50 @@ def _packed_args(b: workloads.Batch, dev):
                    penalty=g.penalty, min_new_tokens=g.min_new_tokens, suppress=g.suppress, eos_id=g.eos_id)
 
 
-def _run_policy(policy, g, kw, dev):
+def _run_policy(policy, g, kw, dev, processed=False):
     flags = torch.zeros(g.B, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    proc = torch.full((g.B, g.V), float("nan"), dtype=torch.float32, device=dev) if processed else None
     with q3s.kernel_policy(policy):
-        ids = q3s.sample_packed(g.logits, g.history, g.offsets, row_flags=flags, error_word=err, **kw)
+        ids = q3s.sample_packed(g.logits, g.history, g.offsets, row_flags=flags, error_word=err, processed=proc,
+                                **kw)
     torch.cuda.synchronize()
-    return ids.cpu().numpy(), flags.cpu().numpy(), int(err.item())
+    out = (ids.cpu().numpy(), flags.cpu().numpy(), int(err.item()))
+    return out + (proc.cpu().numpy(),) if processed else out
+
+
+@pytest.fixture(scope="module")
+def oracle_configs():
+    """The oracle's result per benchmark configuration (computed once)."""
+    cache = {}
+
+    def get(cfg):
+        if cfg not in cache:
+            b = workloads.make_batch(cfg)
+            cache[cfg] = (b, oracle_icdf(b))
+        return cache[cfg]
+    return get
 
 
 @pytest.mark.parametrize("policy", ["warp"] + WARP_POLICIES)
-@pytest.mark.parametrize("cfg,rows", [(1, None), (3, None), (4, (0, 1024))])
-def test_warp_kernel_configs_match_oracle_and_cta(cuda_device, q3s_lib, cfg, rows, policy):
-    b = workloads.make_batch(cfg, rows=rows)
+@pytest.mark.parametrize("cfg", [1, 3, 4])
+def test_warp_kernel_configs_match_oracle_and_cta(cuda_device, q3s_lib, oracle_configs, cfg, policy):
+    """Every row-kernel width on the whole of configs 1, 3 and 4: ids against
+    the oracle and the CTA kernel, processed logits against the oracle within
+    RTOL (1e-5 relative) on every non-boundary row."""
+    b, ref = oracle_configs(cfg)
     g, kw = _packed_args(b, cuda_device)
-    ids_w, kf_w, err_w = _run_policy(policy, g, kw, cuda_device)
+    ids_w, kf_w, err_w, proc_w = _run_policy(policy, g, kw, cuda_device, processed=True)
     ids_c, kf_c, err_c = _run_policy("cta", g, kw, cuda_device)
     assert err_w == 0 and err_c == 0
-    ref = oracle_icdf(b)
     nb, nbm = assert_ids_match(ids_w, ref, kf_w, f"warp config {cfg}", max_frac=MAX_BOUNDARY_FRACTION)
+    ok = ~(ref["boundary"] | ((kf_w & 3) != 0))
+    assert not np.isnan(proc_w).any(), "processed row not fully written"
+    assert _proc_close(proc_w[ok], ref["processed"][ok]), f"{policy} config {cfg}: processed logits differ"
+    # the processed output does not change the sampled ids
+    ids_np, kf_np, _ = _run_policy(policy, g, kw, cuda_device)
+    np.testing.assert_array_equal(ids_np, ids_w)
+    np.testing.assert_array_equal(kf_np, kf_w)
     # both kernel families agree wherever neither flags a boundary
     bnd = ((kf_w | kf_c) & (_lib.ROW_DRAW_BOUNDARY | _lib.ROW_TOPP_BOUNDARY)) != 0
     np.testing.assert_array_equal(ids_w[~bnd], ids_c[~bnd])
@@ -421,14 +446,28 @@ def _warp_case(dev, logits, bf16=False, policy="warp", **kw):
         ref = O.sample_icdf(logits, uniforms=u, temperature=Tv, top_k=kv, top_p=np.full(B, p, np.float32),
                             penalty=np.full(B, pen, np.float32), history=flat[:offs[-1]], offsets=offs,
                             min_new_tokens=np.full(B, mn), suppress=sup, eos_id=eos)
-        flags = torch.zeros(B, dtype=torch.int32, device=dev)
-        err = torch.zeros(1, dtype=torch.int32, device=dev)
-        ids = q3s.sample_packed(x_t.to(dev), _dev(flat, dev), _dev(offs, dev), uniforms=_dev(u, dev),
-                                temperature=_dev(Tv, dev), top_k=_dev(kv, dev), top_p=p, penalty=pen,
-                                min_new_tokens=mn, eos_id=eos, suppress=None if sup is None else _dev(sup, dev),
-                                row_flags=flags, error_word=err)
-        torch.cuda.synchronize()
-        return ids.cpu().numpy(), flags.cpu().numpy(), int(err.item()), ref
+        outs = []
+        for want_proc in (False, True):
+            flags = torch.zeros(B, dtype=torch.int32, device=dev)
+            err = torch.zeros(1, dtype=torch.int32, device=dev)
+            proc = torch.full((B, V), float("nan"), dtype=torch.float32, device=dev) if want_proc else None
+            ids = q3s.sample_packed(x_t.to(dev), _dev(flat, dev), _dev(offs, dev), uniforms=_dev(u, dev),
+                                    temperature=_dev(Tv, dev), top_k=_dev(kv, dev), top_p=p, penalty=pen,
+                                    min_new_tokens=mn, eos_id=eos, suppress=None if sup is None else _dev(sup, dev),
+                                    row_flags=flags, error_word=err, processed=proc)
+            torch.cuda.synchronize()
+            outs.append((ids.cpu().numpy(), flags.cpu().numpy(), int(err.item()),
+                         None if proc is None else proc.cpu().numpy()))
+        (ids, kf, e, _), (ids_p, kf_p, e_p, proc) = outs
+        # the processed-logits variant samples the same ids, and its rows
+        # match the oracle's processed rows wherever no boundary is flagged
+        np.testing.assert_array_equal(ids_p, ids)
+        np.testing.assert_array_equal(kf_p, kf)
+        assert e_p == e
+        ok = ~(ref["boundary"] | ((kf & 3) != 0))
+        assert not np.isnan(proc).any(), "processed row not fully written"
+        assert _proc_close(proc[ok], ref["processed"][ok]), f"{policy}: processed logits differ"
+        return ids, kf, e, ref
 
 
 @pytest.mark.parametrize("V", [1032, 2048, 2056, 3072])
@@ -585,3 +624,87 @@ def test_philox_rows_match_host_generator(cuda_device, q3s_lib):
     got = q3s.philox_rows(77, 257, 15 * 50, step=9, row_keys=_dev(keys, cuda_device)).cpu().numpy()
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
     assert float(got.min()) >= 0.0 and float(got.max()) < 1.0
+    # keys r and r + 2^32 give different streams (all 64 bits of the key)
+    two = q3s.philox_rows(77, 2, 8, row_keys=_dev(np.array([9, 9 + 2**32], np.int64), cuda_device)).cpu().numpy()
+    assert not np.array_equal(two[0], two[1])
+
+
+def test_philox_seeds_match_host_generator(cuda_device, q3s_lib):
+    """One 64-bit seed per row (the reference's per-slot seeds): the device
+    draws the host generator's bits (q3s/philox.py seeded_uniforms) for any
+    seed, step and stage, Gumbel noise within 1e-6."""
+    from q3s import philox as P
+    rng = np.random.default_rng(43)
+    seeds = [int(x) for x in rng.integers(0, 2**63, 300)] + [0, 2**64 - 1, 2**63, 2**32, 2**32 + 1]
+    dseeds = torch.tensor([x - 2**64 if x >= 2**63 else x for x in seeds], dtype=torch.int64, device=cuda_device)
+    for cols, step, stage in ((50, 0, 0), (750, 17, 3), (1, 2**32 - 1, 2**31), (3, 5, 0)):
+        want = P.seeded_uniforms(seeds, cols, step=step, stage=stage)
+        got = q3s.philox_seeds(dseeds, cols, step=step, stage=stage).cpu().numpy()
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+        g = q3s.philox_seeds(dseeds, cols, step=step, stage=stage, kind="gumbel").cpu().numpy()
+        np.testing.assert_allclose(g, P.gumbel_from_uniforms(want), rtol=1e-6, atol=1e-6)
+    # a row's numbers follow its seed, not its position in the batch
+    a = q3s.philox_seeds(dseeds[:8], 50, step=1).cpu().numpy()
+    b = q3s.philox_seeds(dseeds[:8].flip(0), 50, step=1).cpu().numpy()
+    np.testing.assert_array_equal(a, b[::-1])
+
+
+# ---------------------------------------------------------------------------
+# capacity layout of the history (RowHistory): the same ids as packed
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("policy", ["auto", "cta", "w4", "wmax"])
+@pytest.mark.parametrize("cfg", [1, 3])
+def test_capacity_layout_matches_packed_and_oracle(cuda_device, q3s_lib, oracle_configs, cfg, policy):
+    """Rows in regions with spare capacity: ids, flags and processed logits
+    equal the packed layout's, and the oracle's (on the used prefixes)."""
+    b, ref = oracle_configs(cfg)
+    g, kw = _packed_args(b, cuda_device)
+    lens = np.diff(b.offsets.numpy())
+    caps = (lens + np.random.default_rng(cfg).integers(0, 64, b.B)).tolist()
+    rows = q3s.RowHistory.from_packed(g.history, b.offsets, caps, device=cuda_device)
+    outs = {}
+    for name, hk in (("packed", dict(history=g.history, offsets=g.offsets)), ("capacity", rows.sampler_kwargs())):
+        flags = torch.zeros(g.B, dtype=torch.int32, device=cuda_device)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        proc = torch.empty(g.B, g.V, dtype=torch.float32, device=cuda_device)
+        with q3s.kernel_policy(policy):
+            plan = q3s.SamplePlan(g.logits, mode="icdf", processed=proc, row_flags=flags, error_word=err, **hk,
+                                  **{k: v for k, v in kw.items() if k not in ("eos_id", "suppress")},
+                                  suppress_mask=g.suppress, eos_id=g.eos_id)
+            plan.launch()
+        torch.cuda.synchronize()
+        outs[name] = (plan.ids.cpu().numpy(), flags.cpu().numpy(), int(err.item()), proc.cpu().numpy())
+    (ip, fp, ep, pp), (ic, fc, ec, pc) = outs["packed"], outs["capacity"]
+    assert ep == 0 and ec == 0
+    np.testing.assert_array_equal(ic, ip)
+    np.testing.assert_array_equal(fc, fp)
+    np.testing.assert_array_equal(pc, pp)
+    ph, po = rows.packed()
+    ref2 = O.sample_icdf(b.logits, uniforms=b.uniforms.numpy(), temperature=b.temperature.numpy(),
+                         top_k=b.top_k.numpy(), top_p=b.top_p.numpy(), penalty=b.penalty.numpy(),
+                         history=rows.ids.cpu().numpy(), offsets=rows.offsets.cpu().numpy(),
+                         history_lengths=rows.lengths.cpu().numpy(), min_new_tokens=b.min_new_tokens.numpy(),
+                         suppress=b.suppress.numpy(), eos_id=b.eos_id)
+    np.testing.assert_array_equal(ref2["ids"], ref["ids"])
+    np.testing.assert_array_equal(ph.numpy(), b.history.numpy())
+    assert_ids_match(ic, ref2, fc, f"capacity layout config {cfg} {policy}", max_frac=MAX_BOUNDARY_FRACTION)
+
+
+def test_capacity_layout_bad_length_is_reported(cuda_device, q3s_lib):
+    """A length past its region is flagged (OFFSETS) and the row sampled
+    without a history, on both kernel families."""
+    rng = np.random.default_rng(3)
+    B, V = 4, 3072
+    x = torch.from_numpy((rng.standard_normal((B, V)) * 2).astype(np.float32)).to(cuda_device)
+    rows = q3s.RowHistory(B, 16, device=cuda_device)
+    rows.ids.copy_(torch.from_numpy(rng.integers(0, V, rows.ids.numel()).astype(np.int32)))
+    rows.lengths.copy_(torch.tensor([3, 17, 0, 16], dtype=torch.int32))
+    for policy in ("cta", "auto"):
+        err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        with q3s.kernel_policy(policy):
+            plan = q3s.SamplePlan(x, mode="icdf", uniforms=torch.full((B,), 0.5, device=cuda_device), topk=50,
+                                  penalty=1.3, error_word=err, **rows.sampler_kwargs())
+            plan.launch()
+        torch.cuda.synchronize()
+        assert int(err.item()) & _lib.DEVERR_OFFSETS, policy

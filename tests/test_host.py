@@ -204,6 +204,13 @@ def _step_desc(**kw):
           history_out_capacity=104), "overlaps history"),
     (dict(history_out=0x9000, history=0x5000, offsets=0x6000, offsets_out=0x6008, history_len=100,
           history_out_capacity=104), "overlaps offsets"),
+    # capacity layout: the append is in place, into the same buffer
+    (dict(history_lengths=0x8000, history=0x5000, history_out=0x9000, offsets=0x6000,
+          history_out_capacity=64), "history_out == history"),
+    (dict(history_lengths=0x8000, history=0x5000, history_out=0x5000, history_out_capacity=64),
+     "history_out == history"),
+    (dict(history_lengths=0x8000, history=0x5000, history_out=0x5000, offsets=0x6000,
+          history_out_capacity=-1), "outside"),
 ])
 def test_step_update_rejects_bad_arguments_on_host(lib, kw, msg):
     d = _step_desc(**kw)
@@ -216,6 +223,37 @@ def test_step_update_guard_off_and_empty_batch(lib):
     # guard off (abort <= 0): the state arrays are not needed; batch 0 is a no-op
     d = _step_desc(batch=0, abort_frames=0, loop_run=None, input_complete=None)
     assert lib.q3s_step_update(C.byref(d), None) == _lib.OK
+
+
+def test_sample_rejects_history_lengths_without_history(lib):
+    d = _desc(history_lengths=0x8000)
+    assert lib.q3s_sample(C.byref(d), None) == _lib.ERR_INVALID_ARGUMENT
+    assert "history_lengths" in lib.q3s_last_error_string().decode()
+
+
+def test_row_history_round_trips_a_packed_history():
+    """RowHistory.from_packed places each row at the start of its region and
+    packed() gives the packed rows back (host tensors, no GPU)."""
+    import numpy as np
+
+    import q3s
+
+    rng = np.random.default_rng(5)
+    lens = rng.integers(0, 9, 6)
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    hist = rng.integers(0, 3072, int(offs[-1])).astype(np.int32)
+    caps = (lens + rng.integers(0, 4, 6)).tolist()
+    rh = q3s.RowHistory.from_packed(torch.from_numpy(hist), torch.from_numpy(offs), caps, device="cpu")
+    assert rh.offsets.tolist() == np.concatenate([[0], np.cumsum(caps)]).tolist()
+    assert rh.lengths.tolist() == lens.tolist()
+    ph, po = rh.packed()
+    assert ph.tolist() == hist.tolist() and po.tolist() == offs.tolist()
+    for b in range(6):
+        assert rh.ids[rh.offsets[b]:rh.offsets[b] + lens[b]].tolist() == hist[offs[b]:offs[b + 1]].tolist()
+    with pytest.raises(ValueError, match="longer than its capacity"):
+        q3s.RowHistory.from_packed(torch.from_numpy(hist), torch.from_numpy(offs), 0, device="cpu")
+    rh.reset_rows([1, 3])
+    assert rh.lengths.tolist()[1] == 0 and rh.lengths.tolist()[3] == 0
 
 
 def test_python_api_refuses_cpu_tensors():
@@ -302,3 +340,83 @@ def test_rank_failure_surfaces_as_error_not_hang():
     for p in procs:
         p.join(timeout=60)
     assert msgs[0].startswith("error")
+
+
+# ---------------------------------------------------------------------------
+# torch.ops.q3s registration (schemas and Meta kernels need no GPU)
+# ---------------------------------------------------------------------------
+
+def test_torch_ops_register_schemas_and_meta_kernels():
+    import torch
+
+    import q3s
+
+    ops = q3s.load_torch_ops()
+    B, V = 4, 3072
+    meta = dict(device="meta")
+    lg = torch.empty(B, 2, V, dtype=torch.bfloat16, **meta)
+    tc = torch.empty(B, V, dtype=torch.int64, **meta)
+    col = torch.empty(B, 1, **meta)
+    ids, upd = ops.sample_codebook0(lg, tc, torch.empty(B, 50, **meta), col, col, None, 50)
+    assert ids.shape == (B,) and ids.dtype == torch.int64 and upd.shape == (B, V) and upd.dtype == torch.int64
+    assert ops.sample_codebook0_(lg, tc, torch.empty(B, 50, **meta), col, col, None, 50).shape == (B,)
+    i32 = torch.empty(B + 1, dtype=torch.int32, **meta)
+    assert ops.sample_codebook0_packed(lg, i32, i32, *([torch.empty(B, **meta)] * 6), None, 2150).shape == (B,)
+    assert ops.sample_cp_stage(torch.empty(B, 1, 2048, **meta), None, None, 50).shape == (B,)
+    assert ops.sample_cp_frame(torch.empty(15, B, 2048, **meta), col, None, 50).shape == (B, 15)
+    schema = str(ops.sample_codebook0_.default._schema)
+    assert "Tensor(a!) token_counts" in schema
+    for name in ("sample_codebook0", "sample_codebook0_", "sample_codebook0_packed", "sample_cp_stage",
+                 "sample_cp_frame"):
+        assert hasattr(ops, name)
+
+
+def test_torch_ops_have_no_cpu_kernel():
+    import torch
+
+    import q3s
+
+    ops = q3s.load_torch_ops()
+    with pytest.raises(NotImplementedError):
+        ops.sample_cp_stage(torch.zeros(2, 2048), None, None, 50)
+
+
+def test_torch_ops_library_defines_no_libstdcxx_internals():
+    """The operator library must use the process's libstdc++ (a private copy
+    of its locale machinery crashes when an error message is formatted)."""
+    from q3s import build as qbuild
+
+    assert qbuild.TORCH_OPS_PATH.exists()
+    assert qbuild.defined_libstdcxx_internals(qbuild.TORCH_OPS_PATH) == []
+
+
+def test_row_keys_use_all_64_bits():
+    """Keys r and r + 2^32 give different streams; keys below 2^32 keep the
+    counter (j, r, step, 0xA5A5)."""
+    import numpy as np
+
+    from q3s import philox as P
+
+    r = np.array([5, 5 + 2**32, 2**40 + 3], dtype=np.int64)
+    u = P.row_uniforms(11, r, cols=8, step=2)
+    assert not np.array_equal(u[0], u[1])
+    ctr = np.zeros((2, 4), np.uint32)
+    ctr[:, 0] = [0, 1]
+    ctr[:, 1], ctr[:, 2], ctr[:, 3] = 5, 2, 0xA5A5
+    old = P.uint32_to_unit_float(P.philox4x32_10(ctr, np.array([11, 0], np.uint32)).reshape(-1))
+    np.testing.assert_array_equal(u[0], old)
+
+
+def test_seeded_uniforms_depend_only_on_the_row_seed():
+    import numpy as np
+
+    from q3s import philox as P
+
+    seeds = [2**63 + 7, 12345, 2**62, 12345 + 2**32]
+    a = P.seeded_uniforms(seeds, cols=50, step=3, stage=0)
+    b = P.seeded_uniforms(seeds[::-1], cols=50, step=3, stage=0)
+    np.testing.assert_array_equal(a, b[::-1])            # batch position does not matter
+    assert not np.array_equal(a[1], a[3])                 # all 64 bits of the seed
+    assert not np.array_equal(a, P.seeded_uniforms(seeds, cols=50, step=3, stage=1))  # stages differ
+    assert not np.array_equal(a, P.seeded_uniforms(seeds, cols=50, step=4, stage=0))  # steps differ
+    assert a.min() >= 0.0 and a.max() < 1.0

@@ -138,7 +138,10 @@ def _replay_guard(g, i, fn):
     state["frame_idx"][:] = c[:, 0]
     cfg = dict(suspect=int(su), abort=int(ab), emergency=int(em), min_ratio=float(ra), decode_start_frame=c[:, 1],
                text_tokens=c[:, 2], input_complete=c[:, 3])
+    prog = g.get(f"s{i}_progress")
     for t in range(tok.shape[0]):
+        if prog is not None:  # the text count / completion the engine had at this step
+            cfg = dict(cfg, text_tokens=prog[t, :, 0], input_complete=prog[t, :, 1])
         ev, runs = fn(tok[t], state, cfg)
         a = act[t]
         np.testing.assert_array_equal(ev[a], g[f"s{i}_events"][t][a], err_msg=f"scenario {i} step {t}")
