@@ -194,7 +194,8 @@ const char* q3s_last_error_string(void);
 int32_t q3s_abi_version(void);
 
 /* sizeof() of the descriptors as compiled into the library, so a binding can
- * check its own struct layout (which: 0 = sample, 1 = cp_frame, 2 = step). */
+ * check its own struct layout (which: 0 = sample, 1 = cp_frame, 2 = step,
+ * 3 = head). */
 uint32_t q3s_desc_size(int32_t which);
 
 /* Per-row randomness on the device (the next step after the sampler: the
@@ -304,6 +305,35 @@ typedef struct q3s_step_desc {
  * Without the packed copy (history_out NULL, or the capacity layout's
  * in-place append) one thread runs each row. */
 q3s_status q3s_step_update(const q3s_step_desc* desc, void* stream);
+
+/* The codec head and the sampler in one call: logits = hidden @ weight^T on
+ * the tensor cores (bf16 operands, fp32 accumulation, bf16 logits), then --
+ * when `sample` is given -- one q3s_sample step over those logits, launched
+ * behind the head as a programmatic dependent so that its history and
+ * parameter loads overlap the GEMM and it reads the logits while they sit in
+ * L2.  Replaces codec_head(hidden) (scripts/export/talker_unified_modules.py:
+ * 345, nn.Linear(hidden_size, vocab, bias=False) applied to the last
+ * position) or a code predictor's lm_heads[stage] (scripts/export/utils.py:
+ * 1223) followed by the sampling sub-graph (:407-422 / utils.py:1178-1193).
+ * The logits are an output, as the fused engine outputs them. */
+typedef struct q3s_head_desc {
+  uint32_t struct_size;        /* = sizeof(q3s_head_desc) */
+  int32_t batch;               /* B >= 0 (0 = no-op) */
+  int32_t hidden_size;         /* H: a positive multiple of 256 */
+  int32_t vocab;               /* V: a positive multiple of 64, <= Q3S_MAX_VOCAB */
+  const void* hidden;          /* bf16 [B, hidden_row_stride], 16-byte aligned rows */
+  int64_t hidden_row_stride;   /* elements, >= H, a multiple of 8 */
+  const void* weight;          /* bf16 [V, weight_row_stride]: the Linear's weight (out x in) */
+  int64_t weight_row_stride;   /* elements, >= H, a multiple of 8 */
+  void* logits;                /* bf16 [B, logits_row_stride] output */
+  int64_t logits_row_stride;   /* elements, >= V, a multiple of 8 */
+  const q3s_sample_desc* sample; /* optional sampling step over the logits; its batch, vocab, logits,
+                                    logits_dtype and logits_row_stride are taken from here */
+  int32_t* error_word;         /* optional: Q3S_DEVERR_WAIT_TIMEOUT if a bounded device wait gave up */
+  int32_t reserved0;
+} q3s_head_desc;
+
+q3s_status q3s_head_sample(const q3s_head_desc* desc, void* stream);
 
 /* Kernel family for icdf steps that either family can serve (process-wide;
  * a tuning and test knob with no counterpart in the reference interface):

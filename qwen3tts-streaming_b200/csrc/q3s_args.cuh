@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "q3s_sampler.h"
+
 namespace q3s {
 
 struct SampleArgs {
@@ -45,6 +47,7 @@ struct SampleArgs {
   bool vec_counts;
   bool vec_suppress;
   bool vec_history;
+  bool pdl;  // launched as a programmatic dependent: wait for the producing grid before touching logits
 };
 
 struct CpArgs {
@@ -71,7 +74,38 @@ struct CpArgs {
 // V % 8 == 0; `warps` (1, 2, 4 or 8; anything else: the widest variant,
 // 12 warps for V > 2048 and 16 below) warps per row.
 cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st, int warps);
+// q3s_sample's body; `pdl` launches the sampler as a programmatic dependent
+// of the previous kernel on the stream (q3s_sampler.cu).
+q3s_status sample_impl(const q3s_sample_desc* d, cudaStream_t stream, bool pdl);
+// Record a failure for q3s_last_error_string (the calling thread's) and return s.
+q3s_status report(q3s_status s, const char* fmt, ...);
+// SM count of the current device (cached).
+int sm_count();
+
 // Warps per row for a batch size on `sm_count` SMs (0: the widest variant).
 int smem_warps_for(int batch, int sm_count);
+// Launch a kernel with the programmatic-stream-serialization attribute when
+// `pdl` is set (the launch overlaps the previous kernel on the stream, which
+// the kernel waits for with griddepcontrol.wait), plainly otherwise.
+template <typename... Params, typename... Args>
+cudaError_t launch_maybe_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                             Args&&... args) {
+  if (!pdl) {
+    kern<<<grid, block, smem, st>>>(static_cast<Args&&>(args)...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, kern, static_cast<Args&&>(args)...);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
 
 }  // namespace q3s

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -813,6 +814,8 @@ __global__ void __launch_bounds__(NT) sample_rows_kernel(const SampleArgs a) {
   const int V = a.V;
   uint32_t err = 0;
 
+  // launched behind the kernel that writes the logits: wait for it first
+  if (a.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
   // issue every independent load first
   const int shift = a.col_shift ? norm_shift(__ldg(a.col_shift + b), V) : 0;
   float x[E];
@@ -1072,6 +1075,8 @@ __global__ void __launch_bounds__(NT) cp_frame_kernel(const CpArgs a) {
 
 }  // namespace q3s
 
+#include "q3s_cp.cuh"
+
 // ===========================================================================
 // host side: validation, dispatch, C ABI
 // ===========================================================================
@@ -1111,14 +1116,11 @@ bool pick_shape(int V, int& nt, int& e) {
 template <int NT, int E>
 q3s_status launch_rows(const q3s::SampleArgs& a, bool bf16, cudaStream_t st) {
   const bool g = a.mode == Q3S_DRAW_GUMBEL;
-  if (bf16) {
-    if (g) q3s::sample_rows_kernel<NT, E, true, Q3S_DRAW_GUMBEL><<<a.B, NT, 0, st>>>(a);
-    else q3s::sample_rows_kernel<NT, E, true, Q3S_DRAW_ICDF><<<a.B, NT, 0, st>>>(a);
-  } else {
-    if (g) q3s::sample_rows_kernel<NT, E, false, Q3S_DRAW_GUMBEL><<<a.B, NT, 0, st>>>(a);
-    else q3s::sample_rows_kernel<NT, E, false, Q3S_DRAW_ICDF><<<a.B, NT, 0, st>>>(a);
-  }
-  const cudaError_t e = cudaGetLastError();
+  auto kern = bf16 ? (g ? q3s::sample_rows_kernel<NT, E, true, Q3S_DRAW_GUMBEL>
+                        : q3s::sample_rows_kernel<NT, E, true, Q3S_DRAW_ICDF>)
+                   : (g ? q3s::sample_rows_kernel<NT, E, false, Q3S_DRAW_GUMBEL>
+                        : q3s::sample_rows_kernel<NT, E, false, Q3S_DRAW_ICDF>);
+  const cudaError_t e = q3s::launch_maybe_pdl(kern, dim3(a.B), dim3(NT), 0, st, a.pdl, a);
   if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample launch failed: %s", cudaGetErrorString(e));
   return ok();
 }
@@ -1181,6 +1183,20 @@ q3s_status launch_cp(const q3s::CpArgs& a, bool bf16, cudaStream_t st) {
 
 }  // namespace
 
+namespace q3s {
+
+q3s_status report(q3s_status s, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return s;
+}
+
+int sm_count() { return device_sm_count(); }
+
+}  // namespace q3s
+
 extern "C" {
 
 const char* q3s_last_error_string(void) { return g_last_error; }
@@ -1239,6 +1255,7 @@ uint32_t q3s_desc_size(int32_t which) {
   if (which == 0) return static_cast<uint32_t>(sizeof(q3s_sample_desc));
   if (which == 1) return static_cast<uint32_t>(sizeof(q3s_cp_frame_desc));
   if (which == 2) return static_cast<uint32_t>(sizeof(q3s_step_desc));
+  if (which == 3) return static_cast<uint32_t>(sizeof(q3s_head_desc));
   return 0;
 }
 
@@ -1351,6 +1368,14 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
 }
 
 q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
+  return q3s::sample_impl(d, static_cast<cudaStream_t>(stream), false);
+}
+
+}  // extern "C"
+
+namespace q3s {
+
+q3s_status sample_impl(const q3s_sample_desc* d, cudaStream_t stream, bool pdl) {
   if (!d) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample: desc is NULL");
   if (d->struct_size != sizeof(q3s_sample_desc))
     return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample: struct_size %u != %u (ABI mismatch)", d->struct_size,
@@ -1443,8 +1468,9 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
   a.vec_counts = d->token_counts && aligned16(d->token_counts) && (d->token_counts_row_stride % 2 == 0);
   a.vec_suppress = d->suppress_mask && ((reinterpret_cast<uintptr_t>(d->suppress_mask) & 7u) == 0);
   a.vec_history = d->history && aligned16(d->history);
+  a.pdl = pdl;
 
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStream_t st = stream;
   const bool warp_ok = a.mode == Q3S_DRAW_ICDF && !a.token_counts && !a.col_shift &&
                        !a.counts_out && V % 8 == 0 && V > 1024 && V <= 3072 && a.vec_logits &&
                        (!a.suppress || a.vec_suppress);
@@ -1469,6 +1495,10 @@ q3s_status q3s_sample(const q3s_sample_desc* d, void* stream) {
     default: return launch_rows<512, 8>(a, bf16, st);
   }
 }
+
+}  // namespace q3s
+
+extern "C" {
 
 q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
   if (!d) return fail(Q3S_ERR_INVALID_ARGUMENT, "q3s_sample_cp_frame: desc is NULL");
@@ -1542,6 +1572,23 @@ q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
   a.nbuf = a.bulk ? std::max(2, std::min(q3s::MAX_NBUF, static_cast<int>((16u * 1024u) / a.row_bytes))) : 0;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Gumbel / greedy frames with rows of at most 2048 entries: one warp per row
+  // (q3s_cp.cuh); the CTA policy keeps the CTA-per-row kernel
+  const int policy = __atomic_load_n(&g_policy, __ATOMIC_RELAXED);
+  if (a.mode == Q3S_DRAW_GUMBEL && a.bulk && V <= 2048 && a.K <= q3s::CPW_CAP && policy != Q3S_POLICY_CTA) {
+    const size_t dyn = static_cast<size_t>(a.nbuf) * a.row_bytes;
+    auto pick = [&](auto np) {
+      constexpr int NP = decltype(np)::value;
+      return bf16 ? q3s::cp_warp_kernel<NP, true> : q3s::cp_warp_kernel<NP, false>;
+    };
+    void (*kern)(const q3s::CpArgs) = V <= 512    ? pick(std::integral_constant<int, 16>{})
+                                      : V <= 1024 ? pick(std::integral_constant<int, 32>{})
+                                                  : pick(std::integral_constant<int, 64>{});
+    kern<<<a.B, 32, dyn, st>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample_cp_frame launch failed: %s", cudaGetErrorString(e));
+    return ok();
+  }
   if (ne == 16) return launch_cp<512, 16>(a, bf16, st);
   switch (nt) {
     case 64: return launch_cp<64, 8>(a, bf16, st);

@@ -34,8 +34,7 @@ cudaError_t launch_smem(const SampleArgs& a, bool bf16, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     done[v].fetch_or(bit, std::memory_order_release);
   }
-  kern<<<a.B, W * 32, dyn, st>>>(a);
-  return cudaGetLastError();
+  return launch_maybe_pdl(kern, dim3(a.B), dim3(W * 32), dyn, st, a.pdl, a);
 }
 
 template <int R>

@@ -795,11 +795,16 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
   //      overlaps the parameter loads and the history scatter): fp32 rows
   //      straight into the row buffer, bf16 rows into their staging buffer
   //      (kept: the exact values of candidates are read back from it) -------
+  // (launched behind the kernel that writes the logits -- a programmatic
+  //  dependent -- the copy waits until after the history scatter, below)
+  const bool pdl = a.pdl;
   if (t == 0) {
     mbar_init(&sh.bar, 1);
     fence_mbar_init();
-    mbar_expect_tx(&sh.bar, row_bytes);
-    bulk_g2s(BF16 ? static_cast<void*>(stage) : static_cast<void*>(sh.row), grow, row_bytes, &sh.bar);
+    if (!pdl) {
+      mbar_expect_tx(&sh.bar, row_bytes);
+      bulk_g2s(BF16 ? static_cast<void*>(stage) : static_cast<void*>(sh.row), grow, row_bytes, &sh.bar);
+    }
   }
   {
     // zero the histograms and the presence flags (the copy writes neither)
@@ -862,6 +867,15 @@ __global__ void __launch_bounds__(W * 32, row_min_blocks(W, BF16)) sample_smem_k
   }
   const int cur = a.cur_len ? cur_given : hist_len;
   const bool gate = eos_id >= 0 && eos_id < V && cur < min_new;
+  if (pdl) {
+    // the history and parameters are in; now wait for the grid that writes
+    // the logits (its writes are visible after this) and fetch the row
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (t == 0) {
+      mbar_expect_tx(&sh.bar, row_bytes);
+      bulk_g2s(BF16 ? static_cast<void*>(stage) : static_cast<void*>(sh.row), grow, row_bytes, &sh.bar);
+    }
+  }
 
   int id = 0, flags = 0;
   // how the row was finished (read by the processed-logits output only)

@@ -8,7 +8,9 @@ from .step import RowHistory, StepGuard, step_update
 from .ops import (
     CodecSampler,
     CpFramePlan,
+    HeadPlan,
     SamplePlan,
+    head_sample,
     kernel_policy,
     philox_rows,
     philox_seeds,
@@ -24,6 +26,8 @@ from .ops import (
 __all__ = [
     "CodecSampler",
     "CpFramePlan",
+    "HeadPlan",
+    "head_sample",
     "SamplePlan",
     "RowHistory",
     "StepGuard",

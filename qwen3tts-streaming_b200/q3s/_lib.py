@@ -145,6 +145,24 @@ class StepDesc(C.Structure):
     ]
 
 
+class HeadDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("batch", C.c_int32),
+        ("hidden_size", C.c_int32),
+        ("vocab", C.c_int32),
+        ("hidden", _p),
+        ("hidden_row_stride", C.c_int64),
+        ("weight", _p),
+        ("weight_row_stride", C.c_int64),
+        ("logits", _p),
+        ("logits_row_stride", C.c_int64),
+        ("sample", _p),
+        ("error_word", _p),
+        ("reserved0", C.c_int32),
+    ]
+
+
 # every symbol include/q3s_sampler.h declares
 EXPORTS = (
     "q3s_sample",
@@ -156,6 +174,7 @@ EXPORTS = (
     "q3s_philox_rows",
     "q3s_philox_seeds",
     "q3s_step_update",
+    "q3s_head_sample",
 )
 
 _lock = threading.Lock()
@@ -194,9 +213,11 @@ def load(path: str | Path | None = None) -> C.CDLL:
         lib.q3s_philox_seeds.restype = C.c_int
         lib.q3s_step_update.argtypes = [C.POINTER(StepDesc), _p]
         lib.q3s_step_update.restype = C.c_int
+        lib.q3s_head_sample.argtypes = [C.POINTER(HeadDesc), _p]
+        lib.q3s_head_sample.restype = C.c_int
         if lib.q3s_abi_version() != Q3S_ABI_VERSION:
             raise RuntimeError(f"q3s ABI {lib.q3s_abi_version()} != binding {Q3S_ABI_VERSION}; rebuild")
-        for which, st in ((0, SampleDesc), (1, CpFrameDesc), (2, StepDesc)):
+        for which, st in ((0, SampleDesc), (1, CpFrameDesc), (2, StepDesc), (3, HeadDesc)):
             if lib.q3s_desc_size(which) != C.sizeof(st):
                 raise RuntimeError(f"q3s descriptor {st.__name__} size {C.sizeof(st)} != library "
                                    f"{lib.q3s_desc_size(which)}; rebuild")

@@ -364,6 +364,81 @@ class SamplePlan:
         _lib.check(self._lib.q3s_sample(self._ref, _stream_handle(stream)), "q3s_sample")
 
 
+class HeadPlan:
+    """A ready-to-launch ``q3s_head_sample`` call: ``logits = hidden @ weight^T``
+    on the tensor cores (the codec head, talker_unified_modules.py:345, or a
+    code predictor's lm_heads[stage], utils.py:1223), then, with ``sample``
+    (a ``SamplePlan`` bound to the same ``logits`` tensor), that sampling step
+    launched behind the head so that it starts while the GEMM runs and reads
+    the logits from L2.
+
+    ``hidden`` bf16 [B, H] (or [B, S, H]: the last position), ``weight`` bf16
+    [V, H] (``nn.Linear.weight``), ``logits`` bf16 [B, V] (allocated if not
+    given).  H must be a multiple of 256 and V of 64."""
+
+    def __init__(self, hidden: torch.Tensor, weight: torch.Tensor, logits: Optional[torch.Tensor] = None, *,
+                 sample: Optional["SamplePlan"] = None, error_word: Optional[torch.Tensor] = None):
+        lib = _lib.load()
+        self._lib = lib
+        if hidden.dim() == 3:
+            hidden = hidden[:, -1, :]
+        if hidden.dim() != 2 or weight.dim() != 2:
+            raise ValueError("hidden must be [B,H] (or [B,S,H]) and weight [V,H]")
+        dev = hidden.device
+        if dev.type != "cuda":
+            raise RuntimeError("q3s head runs on CUDA tensors only (no CPU fallback)")
+        _need_cuda(weight, "weight", dev)
+        if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+            raise ValueError("hidden and weight must be bf16")
+        if hidden.stride(1) != 1:
+            hidden = hidden.contiguous()
+        if weight.stride(1) != 1:
+            weight = weight.contiguous()
+        B, H = hidden.shape
+        V, H2 = weight.shape
+        if H2 != H:
+            raise ValueError(f"weight is [{V},{H2}] for hidden size {H}")
+        if logits is None:
+            logits = torch.empty(B, V, dtype=torch.bfloat16, device=dev)
+        _need_cuda(logits, "logits", dev)
+        if logits.dtype != torch.bfloat16 or logits.shape != (B, V) or logits.stride(1) != 1:
+            raise ValueError("logits must be bf16 [B,V] with unit column stride")
+        d = _lib.HeadDesc()
+        d.struct_size = C.sizeof(_lib.HeadDesc)
+        d.batch, d.hidden_size, d.vocab = B, H, V
+        d.hidden, d.hidden_row_stride = hidden.data_ptr(), hidden.stride(0) if B > 1 else H
+        d.weight, d.weight_row_stride = weight.data_ptr(), weight.stride(0) if V > 1 else H
+        d.logits, d.logits_row_stride = logits.data_ptr(), logits.stride(0) if B > 1 else V
+        if sample is not None:
+            if sample.desc.logits != logits.data_ptr():
+                raise ValueError("the sample plan must be bound to the head's logits tensor")
+            d.sample = C.addressof(sample.desc)
+        if error_word is not None:
+            _need_cuda(error_word, "error_word", dev)
+            d.error_word = error_word.data_ptr()
+        self.desc = d
+        self._ref = C.byref(d)
+        self._keep = [hidden, weight, logits, sample]
+        self.logits, self.sample, self.error_word = logits, sample, error_word
+        self.ids = sample.ids if sample is not None else None
+        self.device = dev
+
+    def launch(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        _lib.check(self._lib.q3s_head_sample(self._ref, _stream_handle(stream)), "q3s_head_sample")
+
+
+def head_sample(hidden: torch.Tensor, weight: torch.Tensor, **sample_kwargs) -> tuple[torch.Tensor, torch.Tensor]:
+    """``codec_head(hidden)`` and one sampling step over its logits in one call:
+    returns (ids int64 [B], logits bf16 [B, V]).  ``sample_kwargs`` are
+    ``SamplePlan``'s (mode, history / offsets, temperature, top_k, top_p,
+    penalty, uniforms or gumbel_noise, suppress_mask, eos_id, ...)."""
+    h = hidden[:, -1, :] if hidden.dim() == 3 else hidden
+    logits = torch.empty(h.shape[0], weight.shape[0], dtype=torch.bfloat16, device=hidden.device)
+    plan = HeadPlan(hidden, weight, logits, sample=SamplePlan(logits, **sample_kwargs))
+    plan.launch()
+    return plan.ids, logits
+
+
 class CpFramePlan:
     """A ready-to-launch ``q3s_sample_cp_frame`` call (see ``sample_cp_frame``)."""
 

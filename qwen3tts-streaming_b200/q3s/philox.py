@@ -104,7 +104,10 @@ def seeded_uniforms(seeds, cols: int, step: int = 0, stage: int = 0) -> np.ndarr
     (engine/backend/executor.py:79-86, 3216-3254); with that digest as the
     row's seed, a slot's numbers are its seed's alone, whatever batch or
     shard it sits in.  Returns fp32 ``[len(seeds), cols]``."""
-    q = np.asarray([int(x) & 0xFFFFFFFFFFFFFFFF for x in np.atleast_1d(seeds)], dtype=np.uint64)
+    # element by element as Python ints: a list mixing values past 2^63 with
+    # small ones would otherwise become float64 and lose bits
+    it = seeds.tolist() if hasattr(seeds, "tolist") else (seeds if isinstance(seeds, (list, tuple)) else [seeds])
+    q = np.fromiter((int(x) & 0xFFFFFFFFFFFFFFFF for x in it), dtype=np.uint64)
     nblk = (int(cols) + 3) // 4
     ctr = np.zeros((q.shape[0], nblk, 4), dtype=np.uint32)
     ctr[:, :, 0] = np.arange(nblk, dtype=np.uint32)[None, :]

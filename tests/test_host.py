@@ -420,3 +420,54 @@ def test_seeded_uniforms_depend_only_on_the_row_seed():
     assert not np.array_equal(a, P.seeded_uniforms(seeds, cols=50, step=3, stage=1))  # stages differ
     assert not np.array_equal(a, P.seeded_uniforms(seeds, cols=50, step=4, stage=0))  # steps differ
     assert a.min() >= 0.0 and a.max() < 1.0
+
+
+def test_seeded_uniforms_keep_every_bit_of_large_seeds():
+    """Seeds past 2^63 mixed with small ones (a list numpy would turn into
+    float64) and int64 tensors (negative = past 2^63) give the same rows."""
+    import numpy as np
+
+    from q3s import philox as P
+
+    a = P.seeded_uniforms([3, 2**64 - 1, 2**63 + 1], cols=8)
+    b = P.seeded_uniforms(torch.tensor([3, -1, -(2**63) + 1], dtype=torch.int64), cols=8)
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(a[1], P.seeded_uniforms([2**64 - 1], cols=8)[0])
+    assert not np.array_equal(a[1], P.seeded_uniforms([2**64 - 2], cols=8)[0])
+
+
+def _head_desc(**kw):
+    d = _lib.HeadDesc()
+    d.struct_size = C.sizeof(_lib.HeadDesc)
+    d.batch, d.hidden_size, d.vocab = 4, 2048, 3072
+    d.hidden, d.hidden_row_stride = 0x10000, 2048
+    d.weight, d.weight_row_stride = 0x20000, 2048
+    d.logits, d.logits_row_stride = 0x30000, 3072
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(struct_size=8), "struct_size"),
+    (dict(batch=-1), "batch"),
+    (dict(hidden_size=1000), "hidden_size"),
+    (dict(hidden_size=384), "hidden_size"),
+    (dict(vocab=3000), "vocab"),
+    (dict(vocab=3040), "vocab"),
+    (dict(vocab=16384), "vocab"),
+    (dict(logits=None), "required"),
+    (dict(weight=0x20008), "aligned"),
+    (dict(hidden_row_stride=2047), "row strides"),
+    (dict(logits_row_stride=3068), "row strides"),
+])
+def test_head_rejects_bad_arguments_on_host(lib, kw, msg):
+    d = _head_desc(**kw)
+    assert lib.q3s_head_sample(C.byref(d), None) == _lib.ERR_INVALID_ARGUMENT
+    assert msg in lib.q3s_last_error_string().decode()
+
+
+def test_head_empty_batch_is_a_no_op(lib):
+    assert lib.q3s_head_sample(None, None) == _lib.ERR_INVALID_ARGUMENT
+    d = _head_desc(batch=0)
+    assert lib.q3s_head_sample(C.byref(d), None) == _lib.OK
