@@ -1,27 +1,26 @@
-// q3s_cp.cuh -- code-predictor frame, one warp per row: all S stages of the
-// engine graph's stage sampler (CodePredictorUnrolled._select_token,
-// scripts/export/utils.py:1178-1193, looped at :1218-1237) for one row, with
-// no block-wide barrier at all -- a stage is a short chain of warp-synchronous
-// steps, which is what bounds a frame at one row per SM.
+// q3s_cp.cuh -- code-predictor frame for the engine graph's stage sampler
+// (CodePredictorUnrolled._select_token, scripts/export/utils.py:1178-1193,
+// looped at :1218-1237) in Gumbel mode: one CTA of 256 threads per row runs
+// all S stages, each a short fixed chain of seven barriers.
 //
-// Per stage (V <= 2048 entries, NP = V / 32 per lane, lane l holding entries
-// l + 32 i in registers, read from a ring of bulk-copied stage rows with the
-// producer's rotation applied on the read):
-//   greedy (no noise): torch.argmax of the row (lowest index on ties);
-//   Gumbel: exactly-K top-k ordered (value desc, index asc), scores
-//   v / T + noise[rank], argmax (lowest rank on ties):
-//     1. the row maximum (warp shuffles);
-//     2. one histogram of d = max - v in bins 1/8 wide over d < 32 (shared
-//        atomics); a warp scan finds the bin holding the K-th largest --
-//        every entry at or above it falls in that bin or an earlier one
-//        (floor((max - v) * 8) is monotone in v);
-//     3. those entries compacted in index order by ballots (at most 256;
-//        otherwise, or when the K-th lies 32 or more below the maximum, an
-//        exact bitwise select of the K-th key and the first ties by index);
-//     4. each candidate's exact descending rank by all pairs (the list is in
-//        index order, so earlier position = lower index breaks ties);
-//     5. the K ranked candidates' scores, the warp argmax.
-// The noise of the next stage is loaded while the current one computes.
+// A frame is latency-bound (one row per SM at the engine's batch sizes), so
+// a stage does only what exactly-K top-k + Gumbel needs, with thread t
+// holding entries [8t, 8t+8) of the row (read from a ring of bulk-copied
+// stage rows, the producer's rotation applied on the read):
+//   1. the row maximum (warp shuffles, one exchange);
+//   2. one histogram of d = max - v in bins 1/8 wide over d < 32 (shared
+//      atomics; floor((max - v) * 8) is monotone in v, so every entry at or
+//      above the K-th largest lies in the bin holding it or an earlier one);
+//      warp 0 finds that bin and clears what it read;
+//   3. those entries compacted in index order (per-warp ballot counts, one
+//      exchange) -- at most 256 of them, one per thread;
+//   4. each candidate's exact rank (value desc, index asc) by all pairs, up
+//      to 4 threads per candidate; the first K score v / T + noise[rank] (the
+//      noise of this stage was loaded during the previous one); the argmax
+//      (lowest rank on ties).
+// Rows outside that pattern -- the K-th largest 32 or more below the maximum,
+// more than 256 entries down to its bin (massive ties) -- take the general
+// CTA sampler core, which holds the row in the same register layout.
 #pragma once
 
 #include "q3s_args.cuh"
@@ -29,261 +28,258 @@
 
 namespace q3s {
 
-constexpr int CPW_CAP = 256;  // candidate list
+constexpr int CPF_NT = 256;
+constexpr int CPF_E = 8;
+constexpr int CPF_CAP = 256;  // fast-path candidates (one per thread)
 
-// Index of the first entry with the larger value (torch.argmax order).
-Q3S_DEV void warp_argmax_vi(float& v, int& i) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    const float ov = __shfl_xor_sync(FULL, v, o);
-    const int oi = __shfl_xor_sync(FULL, i, o);
-    if (arg_better(ov, oi, v, i)) {
-      v = ov;
-      i = oi;
-    }
-  }
-}
-
-template <int NP, bool BF16>
-__global__ void __launch_bounds__(32) cp_warp_kernel(const CpArgs a) {
-  extern __shared__ __align__(128) unsigned char cpw_ring[];
-  __shared__ __align__(16) uint32_t hist[256];
-  __shared__ float cval[CPW_CAP];
-  __shared__ int cidx[CPW_CAP];
+template <bool BF16>
+__global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
+  constexpr int NT = CPF_NT, E = CPF_E, NW = NT / 32;
+  __shared__ Scratch<NT, E> sh;
   __shared__ __align__(8) uint64_t bars[MAX_NBUF];
-  const int lane = static_cast<int>(threadIdx.x);
-  const int b = static_cast<int>(blockIdx.x);
+  __shared__ float wmax[NW], wbs[NW];
+  __shared__ int wcnt[NW], wbr[NW], wbi[NW];
+  __shared__ int sel[2];
+  extern __shared__ __align__(128) unsigned char cpf_ring[];
+  const int t = static_cast<int>(threadIdx.x), w = t >> 5, lane = t & 31;
+  const int v0 = t * E;
   const int V = a.V, S = a.S, K = a.K;
   const int esz = BF16 ? 2 : 4;
-  const bool greedy = a.noise == nullptr;
-  const uint32_t lt = (1u << lane) - 1u;
+  const int nrows = (a.B - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                    static_cast<int>(gridDim.x);
+  const int nitems = nrows * S;
 
-  auto issue = [&](int j) {
-    const int slot = j % a.nbuf;
+  auto issue = [&](int g) {
+    const int i = g / S, j = g % S;
+    const int b = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
     const unsigned char* src = static_cast<const unsigned char*>(a.logits) +
                                (static_cast<int64_t>(j) * a.stage_stride + static_cast<int64_t>(b) * a.row_stride) * esz;
+    const int slot = g % a.nbuf;
     mbar_expect_tx(&bars[slot], a.row_bytes);
-    bulk_g2s(cpw_ring + static_cast<size_t>(slot) * a.row_bytes, src, a.row_bytes, &bars[slot]);
+    bulk_g2s(cpf_ring + static_cast<size_t>(slot) * a.row_bytes, src, a.row_bytes, &bars[slot]);
   };
-  if (lane == 0) {
+  // noise of item g (row i, stage j) by rank into half (g & 1) of sh.noise
+  auto load_noise = [&](int g) {
+    if (g >= nitems || t >= K) return;
+    const int i = g / S, j = g % S;
+    const int b = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+    sh.noise[(g & 1) * CPF_CAP + t] =
+        __ldg(a.noise + static_cast<int64_t>(b) * a.noise_row_stride + static_cast<int64_t>(j) * a.noise_stage_stride + t);
+  };
+
+  clear_hist<NT, E>(sh);
+  if (t == 0) {
     for (int s = 0; s < a.nbuf; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
-    for (int j = 0; j < min(a.nbuf, S); ++j) issue(j);
   }
-  __syncwarp();
+  load_noise(0);
+  __syncthreads();
+  if (t == 0)
+    for (int g = 0; g < min(a.nbuf, nitems); ++g) issue(g);
 
-  int64_t prev = (a.producer == Q3S_CP_ROTATE) ? __ldg(a.ids_init + b) : 0;
-  const float T = a.temperature ? __ldg(a.temperature + b) : a.temperature_default;
-  constexpr int KP = CPW_CAP / 32;  // noise values per lane (K <= CPW_CAP)
-  float gz[KP];
-  auto load_noise = [&](int j) {
-#pragma unroll
-    for (int q = 0; q < KP; ++q) {
-      const int r = lane + 32 * q;
-      gz[q] = (!greedy && r < K) ? __ldg(a.noise + static_cast<int64_t>(b) * a.noise_row_stride +
-                                         static_cast<int64_t>(j) * a.noise_stage_stride + r)
-                                 : 0.0f;
-    }
-  };
-  if (!greedy) load_noise(0);
-
-  for (int j = 0; j < S; ++j) {
-    const int slot = j % a.nbuf;
-    const int shift = (a.producer == Q3S_CP_ROTATE) ? norm_shift(prev, V) : 0;
-    if (!__all_sync(FULL, mbar_wait_bounded(&bars[slot], static_cast<uint32_t>((j / a.nbuf) & 1)))) {
-      // give up: report, wait (bounded) for the copies still in flight, leave
-      if (lane == 0) {
-        if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
-        for (int h = j; h < min(j + a.nbuf, S); ++h)
-          (void)mbar_wait_bounded(&bars[h % a.nbuf], static_cast<uint32_t>((h / a.nbuf) & 1));
+  for (int i = 0; i < nrows; ++i) {
+    const int b = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+    int64_t prev = (a.producer == Q3S_CP_ROTATE) ? __ldg(a.ids_init + b) : 0;
+    const float T = a.temperature ? __ldg(a.temperature + b) : a.temperature_default;
+    for (int j = 0; j < S; ++j) {
+      const int g = i * S + j;
+      const int shift = (a.producer == Q3S_CP_ROTATE) ? norm_shift(prev, V) : 0;
+      const int slot = g % a.nbuf;
+      const bool ok = mbar_wait_bounded(&bars[slot], static_cast<uint32_t>((g / a.nbuf) & 1));
+      if (__syncthreads_or(!ok)) {  // (barrier 0) give up: report, wait (bounded) for copies in flight
+        if (t == 0) {
+          if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
+          const int issued = g == 0 ? a.nbuf : a.nbuf - 1;
+          for (int h = g; h < min(g + issued, nitems); ++h)
+            (void)mbar_wait_bounded(&bars[h % a.nbuf], static_cast<uint32_t>((h / a.nbuf) & 1));
+        }
+        return;
       }
-      return;
-    }
-    const unsigned char* row = cpw_ring + static_cast<size_t>(slot) * a.row_bytes;
-    float x[NP];
+      // every thread is past the previous stage: refill its slot, prefetch
+      // the next stage's noise
+      if (t == 0 && g > 0 && g - 1 + a.nbuf < nitems) issue(g - 1 + a.nbuf);
+      load_noise(g + 1);
+      const unsigned char* row = cpf_ring + static_cast<size_t>(slot) * a.row_bytes;
+      float x[E];
+      uint32_t vmask = 0;
 #pragma unroll
-    for (int i = 0; i < NP; ++i) {
-      const int v = lane + 32 * i;
-      int q = v + shift;
-      q -= q >= V ? V : 0;
-      x[i] = v < V ? (BF16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(row)[q])
-                           : reinterpret_cast<const float*>(row)[q])
-                   : -INFINITY;
-    }
-    __syncwarp();
-    if (lane == 0 && j + a.nbuf < S) issue(j + a.nbuf);  // every lane has read the slot
-
-    int id = 0, flags = 0;
-    float gcur[KP];
-#pragma unroll
-    for (int q = 0; q < KP; ++q) gcur[q] = gz[q];
-    if (!greedy && j + 1 < S) load_noise(j + 1);  // in flight while this stage computes
-    if (greedy) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < NP; ++i) {
-        const int v = lane + 32 * i;
-        if (v < V && arg_better(x[i], v, bv, bi)) {
-          bv = x[i];
-          bi = v;
+      for (int e = 0; e < E; ++e) {
+        const int v = v0 + e;
+        x[e] = -INFINITY;
+        if (v < V) {
+          int q = v + shift;
+          q -= q >= V ? V : 0;
+          x[e] = BF16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(row)[q])
+                      : reinterpret_cast<const float*>(row)[q];
+          vmask |= 1u << e;
         }
       }
-      warp_argmax_vi(bv, bi);
-      id = bi;
-      flags = Q3S_ROW_GREEDY;
-    } else {
+
+      // 1. the row maximum
       float m = x[0];
 #pragma unroll
-      for (int i = 1; i < NP; ++i) m = fmaxf(m, x[i]);
+      for (int e = 1; e < E; ++e) m = fmaxf(m, x[e]);
       m = warp_max_f(m);
-      // histogram of floor((m - v) * 8) over d < 32
-      reinterpret_cast<uint4*>(hist)[2 * lane] = make_uint4(0, 0, 0, 0);
-      reinterpret_cast<uint4*>(hist)[2 * lane + 1] = make_uint4(0, 0, 0, 0);
-      __syncwarp();
+      if (lane == 0) wmax[w] = m;
+      __syncthreads();  // (1)
+      m = wmax[0];
 #pragma unroll
-      for (int i = 0; i < NP; ++i) {
-        const float e = __fmul_rn(__fsub_rn(m, x[i]), 8.0f);
-        if (e < 256.0f) atomicAdd(&hist[static_cast<uint32_t>(e)], 1u);
+      for (int k = 1; k < NW; ++k) m = fmaxf(m, wmax[k]);
+      // 2. histogram of floor((m - v) * 8) over d < 32
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float ev = __fmul_rn(__fsub_rn(m, x[e]), 8.0f);
+        if (ev < 256.0f) atomicAdd(&sh.hist[0][static_cast<uint32_t>(ev)], 1u);
       }
-      __syncwarp();
-      // the bin of the K-th largest: bins ascending in d = descending values
-      const uint4 h0 = reinterpret_cast<const uint4*>(hist)[2 * lane];
-      const uint4 h1 = reinterpret_cast<const uint4*>(hist)[2 * lane + 1];
-      const uint32_t c[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-      uint32_t sum = 0;
+      __syncthreads();  // (2)
+      if (w == 0) {
+        uint4* hb = reinterpret_cast<uint4*>(sh.hist[0]) + 2 * lane;
+        const uint4 h0 = hb[0], h1 = hb[1];
+        hb[0] = make_uint4(0, 0, 0, 0);  // the histogram's zero invariant
+        hb[1] = make_uint4(0, 0, 0, 0);
+        const uint32_t c[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        uint32_t sum = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum += c[i];
-      uint32_t inc = sum;
+        for (int k = 0; k < 8; ++k) sum += c[k];
+        uint32_t inc = sum;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(FULL, inc, o);
-        if (lane >= o) inc += y;
-      }
-      const uint32_t kk = static_cast<uint32_t>(K);
-      const unsigned hitb = __ballot_sync(FULL, inc >= kk && inc - sum < kk);
-      int bK = 256;
-      uint32_t cnt = 0;
-      if (hitb) {
-        const int src = __ffs(hitb) - 1;
-        int mb = 0;
-        uint32_t mc = 0;
-        if (lane == src) {
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(FULL, inc, o);
+          if (lane >= o) inc += y;
+        }
+        const uint32_t kk = static_cast<uint32_t>(K);
+        const unsigned hit = __ballot_sync(FULL, inc >= kk && inc - sum < kk);
+        if (lane == 0) {
+          sel[0] = 256;
+          sel[1] = 0;
+        }
+        __syncwarp();
+        if (hit && lane == __ffs(hit) - 1) {
           uint32_t acc = inc - sum;
-          bool found = false;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            acc += c[i];
-            if (!found && acc >= kk) {
-              found = true;
-              mb = 8 * lane + i;
-              mc = acc;
+          for (int k = 0; k < 8; ++k) {
+            acc += c[k];
+            if (acc >= kk) {
+              sel[0] = 8 * lane + k;
+              sel[1] = static_cast<int>(acc);
+              break;
             }
           }
         }
-        bK = __shfl_sync(FULL, mb, src);
-        cnt = __shfl_sync(FULL, mc, src);
       }
-      int n = 0;
-      if (bK < 256 && cnt <= static_cast<uint32_t>(CPW_CAP)) {
-        // candidates: every entry in bins 0..bK, in index order
-#pragma unroll
-        for (int i = 0; i < NP; ++i) {
-          const float e = __fmul_rn(__fsub_rn(m, x[i]), 8.0f);
-          const bool cnd = lane + 32 * i < V && e < static_cast<float>(bK + 1);
-          const unsigned bal = __ballot_sync(FULL, cnd);
-          if (cnd) {
-            const int p = n + __popc(bal & lt);
-            cval[p] = x[i];
-            cidx[p] = lane + 32 * i;
-          }
-          n += __popc(bal);
+      __syncthreads();  // (3)
+      const int bK = sel[0], n = sel[1];
+      int id, flags = 0;
+      if (bK >= 256 || n > CPF_CAP) {
+        // outside the fast pattern: the general CTA core on the same registers
+        RowCfg c;
+        c.mode = Q3S_DRAW_GUMBEL;
+        c.greedy = false;
+        c.T = T;
+        c.k = K;
+        c.top_p = 1.0f;
+        c.u = 0.0f;
+        c.noise = a.noise + static_cast<int64_t>(b) * a.noise_row_stride + static_cast<int64_t>(j) * a.noise_stage_stride;
+        uint32_t err = 0;
+        id = sample_core<NT, E, Q3S_DRAW_GUMBEL>(x, vmask, 0u, 1.0f, V, c, sh, nullptr, flags, err);
+        if (err && a.error_word) atomicOr(a.error_word, static_cast<int>(err));
+        // every thread holds the same id; the owner (complete flags) writes it
+        if (id >= v0 && id < v0 + E) {
+          a.ids_out[static_cast<int64_t>(b) * S + j] = id;
+          if (a.row_flags) a.row_flags[static_cast<int64_t>(b) * S + j] = flags;
         }
-      } else {
-        // exact: the K-th largest key bit by bit, then the entries above it
-        // and the first ties by index (exactly K of them)
-        uint32_t key[NP];
-#pragma unroll
-        for (int i = 0; i < NP; ++i) key[i] = lane + 32 * i < V ? f2key(x[i]) : 0u;
-        uint32_t prefix = 0;
-#pragma unroll 1
-        for (int bit = 31; bit >= 0; --bit) {
-          const uint32_t want = prefix | (1u << bit);
-          uint32_t ge = 0;
-#pragma unroll
-          for (int i = 0; i < NP; ++i) ge += key[i] >= want;
-#pragma unroll
-          for (int o = 16; o; o >>= 1) ge += __shfl_xor_sync(FULL, ge, o);
-          if (ge >= kk) prefix = want;  // the K-th largest key is >= want
-        }
-        uint32_t above = 0;
-#pragma unroll
-        for (int i = 0; i < NP; ++i) above += key[i] > prefix;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) above += __shfl_xor_sync(FULL, above, o);
-        int ties = 0;
-#pragma unroll
-        for (int i = 0; i < NP; ++i) {
-          const bool over = key[i] > prefix, tie = lane + 32 * i < V && key[i] == prefix;
-          const unsigned bt = __ballot_sync(FULL, tie);
-          const bool take = over || (tie && ties + __popc(bt & lt) < K - static_cast<int>(above));
-          const unsigned bal = __ballot_sync(FULL, take);
-          if (take) {
-            const int p = n + __popc(bal & lt);
-            cval[p] = x[i];
-            cidx[p] = lane + 32 * i;
-          }
-          n += __popc(bal);
-          ties += __popc(bt);
-        }
+        prev = id;
+        // the core loads its own noise into sh.noise[0, K): load the next
+        // stage's again once every thread is done with the core
+        __syncthreads();
+        load_noise(g + 1);
+        continue;
       }
-      __syncwarp();
-      // exact descending ranks by all pairs; scores of the first K; argmax
+      // 3. candidates (bins 0..bK) in index order
+      uint32_t cm = 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float ev = __fmul_rn(__fsub_rn(m, x[e]), 8.0f);
+        cm |= ((v0 + e < V && ev < static_cast<float>(bK + 1)) ? 1u : 0u) << e;
+      }
+      const uint32_t cnt = __popc(cm);
+      uint32_t incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (lane == 31) wcnt[w] = static_cast<int>(incl);
+      __syncthreads();  // (4)
+      int p = static_cast<int>(incl - cnt);
+      for (int k = 0; k < w; ++k) p += wcnt[k];
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if ((cm >> e) & 1u) {
+          sh.xs[p] = x[e];
+          sh.cand[p].y = static_cast<uint32_t>(v0 + e);
+          ++p;
+        }
+      __syncthreads();  // (5)
+      // 4. ranks (LP threads per candidate, each counting over every LP-th
+      //    group of four), scores, argmax (lowest rank on ties)
       float bs = -INFINITY;
-      int br = 0x7fffffff, bidx = 0;
-      for (int pb = 0; pb < n; pb += 32) {
-        const int p = pb + lane;
+      int br = 0x7fffffff, bi = 0;
+      {
+        const int LP = n <= 64 ? 4 : (n <= 128 ? 2 : 1);
+        const int p = t / LP, sub = t % LP;
         const bool act = p < n;
-        const float vp = act ? cval[p] : 0.0f;
+        const float vp = act ? sh.xs[p] : 0.0f;
+        const int n4 = (n + 3) >> 2;
         int r = 0;
         if (act)
-          for (int q = 0; q < n; ++q) {
-            const float vq = cval[q];
-            r += (vq > vp) || (vq == vp && q < p);
+          for (int q4 = sub; q4 < n4; q4 += LP) {
+            const float4 f = reinterpret_cast<const float4*>(sh.xs)[q4];
+            const int q = 4 * q4;
+            r += (q < n) && ((f.x > vp) || (f.x == vp && q < p));
+            r += (q + 1 < n) && ((f.y > vp) || (f.y == vp && q + 1 < p));
+            r += (q + 2 < n) && ((f.z > vp) || (f.z == vp && q + 2 < p));
+            r += (q + 3 < n) && ((f.w > vp) || (f.w == vp && q + 3 < p));
           }
-        float g = 0.0f;
-#pragma unroll
-        for (int q = 0; q < KP; ++q) {
-          const float gv = __shfl_sync(FULL, gcur[q], r & 31);
-          if (q == (r >> 5)) g = gv;
-        }
-        if (act && r < K) {
-          const float s = __fadd_rn(__fdiv_rn(vp, T), g);
-          if (s > bs || (s == bs && r < br)) {
-            bs = s;
-            br = r;
-            bidx = cidx[p];
-          }
+        for (int o = 1; o < LP; o <<= 1) r += __shfl_xor_sync(FULL, r, o);
+        if (act && sub == 0 && r < K) {
+          bs = __fadd_rn(__fdiv_rn(vp, T), sh.noise[(g & 1) * CPF_CAP + r]);
+          br = r;
+          bi = static_cast<int>(sh.cand[p].y);
         }
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
         const float os = __shfl_xor_sync(FULL, bs, o);
-        const int orr = __shfl_xor_sync(FULL, br, o), oi = __shfl_xor_sync(FULL, bidx, o);
+        const int orr = __shfl_xor_sync(FULL, br, o), oi = __shfl_xor_sync(FULL, bi, o);
         if (os > bs || (os == bs && orr < br)) {
           bs = os;
           br = orr;
-          bidx = oi;
+          bi = oi;
         }
       }
-      id = bidx;
-      __syncwarp();  // the candidate list and histogram are reused next stage
+      if (lane == 0) {
+        wbs[w] = bs;
+        wbr[w] = br;
+        wbi[w] = bi;
+      }
+      __syncthreads();  // (6)
+      bs = wbs[0];
+      br = wbr[0];
+      id = wbi[0];
+#pragma unroll
+      for (int k = 1; k < NW; ++k)
+        if (wbs[k] > bs || (wbs[k] == bs && wbr[k] < br)) {
+          bs = wbs[k];
+          br = wbr[k];
+          id = wbi[k];
+        }
+      if (t == 0) {
+        a.ids_out[static_cast<int64_t>(b) * S + j] = id;
+        if (a.row_flags) a.row_flags[static_cast<int64_t>(b) * S + j] = 0;
+      }
+      prev = id;
     }
-    if (lane == 0) {
-      a.ids_out[static_cast<int64_t>(b) * S + j] = id;
-      if (a.row_flags) a.row_flags[static_cast<int64_t>(b) * S + j] = flags;
-    }
-    prev = id;
   }
 }
 

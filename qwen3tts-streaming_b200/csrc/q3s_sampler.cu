@@ -1572,19 +1572,19 @@ q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
   a.nbuf = a.bulk ? std::max(2, std::min(q3s::MAX_NBUF, static_cast<int>((16u * 1024u) / a.row_bytes))) : 0;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Gumbel / greedy frames with rows of at most 2048 entries: one warp per row
-  // (q3s_cp.cuh); the CTA policy keeps the CTA-per-row kernel
+  // Gumbel frames (the engine graph's stages) with rows of at most 2048
+  // entries and K <= 256: the lean stage chain of q3s_cp.cuh; the CTA policy
+  // keeps the general CTA-per-row kernel
   const int policy = __atomic_load_n(&g_policy, __ATOMIC_RELAXED);
-  if (a.mode == Q3S_DRAW_GUMBEL && a.bulk && V <= 2048 && a.K <= q3s::CPW_CAP && policy != Q3S_POLICY_CTA) {
+  if (a.mode == Q3S_DRAW_GUMBEL && a.noise && a.bulk && V <= q3s::CPF_NT * q3s::CPF_E && a.K <= q3s::CPF_CAP &&
+      policy != Q3S_POLICY_CTA) {
     const size_t dyn = static_cast<size_t>(a.nbuf) * a.row_bytes;
-    auto pick = [&](auto np) {
-      constexpr int NP = decltype(np)::value;
-      return bf16 ? q3s::cp_warp_kernel<NP, true> : q3s::cp_warp_kernel<NP, false>;
-    };
-    void (*kern)(const q3s::CpArgs) = V <= 512    ? pick(std::integral_constant<int, 16>{})
-                                      : V <= 1024 ? pick(std::integral_constant<int, 32>{})
-                                                  : pick(std::integral_constant<int, 64>{});
-    kern<<<a.B, 32, dyn, st>>>(a);
+    auto kern = bf16 ? q3s::cp_fast_kernel<true> : q3s::cp_fast_kernel<false>;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, q3s::CPF_NT, dyn) != cudaSuccess || per_sm <= 0)
+      per_sm = 1;
+    const int grid = std::min(a.B, device_sm_count() * per_sm);
+    kern<<<grid, q3s::CPF_NT, dyn, st>>>(a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample_cp_frame launch failed: %s", cudaGetErrorString(e));
     return ok();

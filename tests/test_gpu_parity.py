@@ -363,6 +363,48 @@ def test_cp_frame_equals_fifteen_single_stage_launches(cuda_device, q3s_lib):
     np.testing.assert_array_equal(torch.stack(outs, 1).cpu().numpy(), frame.cpu().numpy())
 
 
+@pytest.mark.parametrize("case", ["ties", "spread", "mixed", "fp32"])
+def test_cp_frame_fast_path_and_its_fallbacks(cuda_device, q3s_lib, case):
+    """The Gumbel frame kernel (auto policy) against the oracle chain and the
+    CTA-per-row frame kernel, on rows that leave its fast pattern: massive
+    ties (more than 256 entries down to the K-th's bin) and widely spread
+    values (the K-th 32 or more below the maximum), alone and mixed with
+    ordinary rows, bf16 and fp32."""
+    rng = np.random.default_rng({"ties": 1, "spread": 2, "mixed": 3, "fp32": 4}[case])
+    S, B, V = 5, 40, 2048
+    base = (rng.standard_normal((S, B, V)) * 2.5).astype(np.float32)
+    if case in ("ties", "mixed"):
+        rows = slice(None) if case == "ties" else slice(0, B, 3)
+        base[:, rows, :] = np.round(base[:, rows, :] * 2) / 2  # a few hundred entries share each top value
+        base[:, rows, :600] = np.maximum(base[:, rows, :600], 4.0)
+    if case in ("spread", "mixed"):
+        rows = slice(None) if case == "spread" else slice(1, B, 3)
+        base[:, rows, :] *= 40.0
+    bf16 = case != "fp32"
+    bt = torch.from_numpy(base)
+    if bf16:
+        bt = bt.to(torch.bfloat16)
+        base = bt.float().numpy()
+    init = rng.integers(0, V, B)
+    T = rng.uniform(0.6, 1.0, B).astype(np.float32)
+    u = rng.random((B, S, 50)).astype(np.float32)
+    from q3s.philox import gumbel_from_uniforms
+    noise = gumbel_from_uniforms(u)
+    ref = O.cp_frame(base, mode="gumbel", ids_init=init, rotate=True, temperature=T, gumbel_noise=noise)
+    outs = {}
+    for policy in ("auto", "cta"):
+        err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        with q3s.kernel_policy(policy):
+            ids = q3s.sample_cp_frame(bt.to(cuda_device), mode="gumbel", ids_init=_dev(init, cuda_device), rotate=True,
+                                      temperature=_dev(T, cuda_device), topk=50,
+                                      gumbel_noise=_dev(noise, cuda_device), error_word=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0, policy
+        outs[policy] = ids.cpu().numpy()
+    np.testing.assert_array_equal(outs["auto"], ref["ids"])
+    np.testing.assert_array_equal(outs["cta"], ref["ids"])
+
+
 # ---------------------------------------------------------------------------
 # warp-per-row kernels (forced by policy; "auto" picks them for large batches)
 # ---------------------------------------------------------------------------
