@@ -117,13 +117,12 @@ int max_active_clusters() {
 struct HeadCfg {
   int ks, bn;
 };
-constexpr HeadCfg kHeadCfgs[] = {{4, 64}, {4, 96}, {4, 128}, {8, 128}, {8, 192}, {8, 256}};
+constexpr HeadCfg kHeadCfgs[] = {{4, 64}, {4, 96}, {4, 128}, {8, 128}, {8, 192}};
 
 int max_active(const HeadCfg& c) {
   if (c.ks == 4) return c.bn == 64 ? max_active_clusters<4, 64>() : c.bn == 96 ? max_active_clusters<4, 96>()
                                                                                : max_active_clusters<4, 128>();
-  return c.bn == 128 ? max_active_clusters<8, 128>() : c.bn == 192 ? max_active_clusters<8, 192>()
-                                                                   : max_active_clusters<8, 256>();
+  return c.bn == 128 ? max_active_clusters<8, 128>() : max_active_clusters<8, 192>();
 }
 
 // The first configuration (in preference order) that divides the problem and
@@ -197,8 +196,7 @@ extern "C" q3s_status q3s_head_sample(const q3s_head_desc* d, void* stream) {
                      : launch_head<4, 128>(tm_hidden, tm_weight, a, mtiles, st);
   else
     e = cfg.bn == 128 ? launch_head<8, 128>(tm_hidden, tm_weight, a, mtiles, st)
-      : cfg.bn == 192 ? launch_head<8, 192>(tm_hidden, tm_weight, a, mtiles, st)
-                      : launch_head<8, 256>(tm_hidden, tm_weight, a, mtiles, st);
+                      : launch_head<8, 192>(tm_hidden, tm_weight, a, mtiles, st);
   if (e != cudaSuccess) return report(Q3S_ERR_CUDA, "q3s_head_sample: head launch failed: %s", cudaGetErrorString(e));
   if (!d->sample) return report(Q3S_OK, "");
 

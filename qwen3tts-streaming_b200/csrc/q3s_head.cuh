@@ -9,26 +9,35 @@
 // vocabulary tile over 1/KS of the hidden dimension (split-K), and the KS
 // CTAs of a cluster -- one per K slice -- add their partial tiles through
 // distributed shared memory in a fixed order (so the sums are reproducible),
-// each CTA finishing 128 / KS of the 128 rows.  The split costs a partial tile
-// per CTA on the cluster's network, so KS = 4 where it fills the GPU: for
-// V = 3072, BN = 96 and 32 x 4 = 128 CTAs per 128 rows, 224 KB of operands
-// and a 48 KB partial tile each (KS = 8 and BN up to 256 for other shapes).
+// each CTA finishing 128 / KS of the 128 rows.  For V = 3072: KS = 4, BN = 96,
+// 32 x 4 = 128 CTAs per 128 rows, 224 KB of operands each.
 //
 // Per CTA (128 threads):
 //   warp 0 lane 0   TMA producer: 2-D tiled loads (cp.async.bulk.tensor, no
 //                   multicast) of the hidden tile [128 x 64] and the weight
-//                   tile [256 x 64] per K chunk into a 4-stage ring, 128-byte
-//                   swizzled (the layout the MMA descriptors below name);
+//                   tile [BN x 64] per K chunk into a ring of as many stages
+//                   as shared memory holds (5-8: most of a CTA's operands are
+//                   in flight at once), 128-byte swizzled (the layout the MMA
+//                   descriptors below name);
 //   warp 1 lane 0   MMA issuer: tcgen05.mma.cta_group::1.kind::f16 (bf16 x
-//                   bf16 -> fp32), M = 128, N = 256, K = 16 per instruction,
-//                   accumulator in TMEM (256 columns); tcgen05.commit frees a
-//                   stage and finally signals the epilogue;
-//   all 4 warps     epilogue: a cluster barrier (every CTA is past its MMAs,
-//                   so every ring can receive); tcgen05.ld of their 32 TMEM
-//                   lanes (rows), each row stored straight into the ring of
-//                   the CTA that finishes it (st.shared::cluster, slot = this
-//                   CTA's K slice); a cluster barrier; the fixed-order sum of
-//                   the 8 slices from local shared memory, rounded to bf16.
+//                   bf16 -> fp32), M = 128, N = BN, K = 16 per instruction,
+//                   accumulator in TMEM; tcgen05.commit frees a stage and
+//                   finally signals the epilogue;
+//   each warp       epilogue, independently: tcgen05.ld of its 32 TMEM lanes
+//                   (rows) into a staging copy of the partial tile in the
+//                   now idle ring, then one bulk copy per owning CTA
+//                   (cp.async.bulk shared::cta -> shared::cluster, completing
+//                   on the owner's receive mbarrier) of the rows that CTA
+//                   finishes;
+//   all threads     wait for the KS - 1 incoming slices on the receive
+//                   mbarrier, then the fixed-order sum of the KS slices
+//                   (slice k from CTA k; this CTA's own from its staging),
+//                   rounded to bf16.
+// No cluster-wide barrier sits on the critical path: one after the barrier
+// initialisation (a remote mbarrier must be initialised before a copy
+// completes on it; every CTA has long passed it when its copies go out) and
+// one before exit (every copy into every CTA of the cluster has landed, so no
+// CTA leaves while a copy still reads its staging), split around the sum.
 //
 // Every mbarrier wait is bounded; a wait that gives up sets
 // Q3S_DEVERR_WAIT_TIMEOUT, waits (bounded) for this CTA's own copies and MMAs,
@@ -47,9 +56,16 @@ namespace q3s {
 
 constexpr int HEAD_BM = 128;      // rows per tile (MMA M)
 constexpr int HEAD_BK = 64;       // K per chunk: one 128-byte swizzled row of bf16
-constexpr int HEAD_STAGES = 4;
+constexpr int HEAD_MAX_STAGES = 8;
 constexpr int HEAD_NT = 128;
 constexpr int HEAD_A_BYTES = HEAD_BM * HEAD_BK * 2;   // 16 KB
+constexpr int HEAD_BAR_BYTES = 256;
+constexpr int HEAD_SMEM_LIMIT = 227 * 1024;     // per CTA
+// Preferred budget: leaves an SM room for one CTA of the row sampler launched
+// behind the head as a programmatic dependent (~27 KB of shared memory and
+// 384 threads at V = 3072), which then runs its preparation while the head
+// still computes and starts on the logits the moment the head's grid is done.
+constexpr int HEAD_SMEM_SHARED = 192 * 1024;
 
 // One configuration: KS CTAs per cluster (one K slice each, 4 or 8) and a
 // vocabulary tile of BN entries (the MMA's N).
@@ -59,17 +75,22 @@ struct HeadTile {
   static constexpr int TMEM_COLS = BN <= 128 ? 128 : 256;       // power of two >= BN
   static constexpr int B_BYTES = BN * HEAD_BK * 2;
   static constexpr int STAGE_BYTES = HEAD_A_BYTES + B_BYTES;   // multiple of 1024
-  static constexpr int RING_BYTES = HEAD_STAGES * STAGE_BYTES;
-  static constexpr int RSTRIDE = BN + 4;                        // fp32 receive-row stride (16-byte rows, no bank conflicts)
-  static constexpr int RECV_BYTES = KS * ROWS * RSTRIDE * 4;
-  static constexpr int STG_STRIDE = 36;                         // staging row stride (32 columns + pad), floats
-  static constexpr int STG_BYTES = HEAD_BM * STG_STRIDE * 4;    // one 32-column chunk of the accumulator
-  static constexpr int BUF_BYTES = RECV_BYTES + STG_BYTES > RING_BYTES ? RECV_BYTES + STG_BYTES : RING_BYTES;
-  static constexpr int SMEM_BYTES = 1024 + BUF_BYTES + 256;    // alignment slack, ring / receive, barriers
+  static constexpr int SLOT_BYTES = ROWS * BN * 4;              // one K slice of the rows a CTA finishes
+  static constexpr int RECV_BYTES = (KS - 1) * SLOT_BYTES;      // the other CTAs' slices
+  static constexpr int STAGING_BYTES = HEAD_BM * BN * 4;        // this CTA's whole partial tile (in the ring)
+  static constexpr int fit(int limit) { return (limit - 1024 - HEAD_BAR_BYTES - RECV_BYTES) / STAGE_BYTES; }
+  // the shared budget when it still holds 3 stages and the staging copy
+  static constexpr bool SHARED_OK = fit(HEAD_SMEM_SHARED) >= 3 && fit(HEAD_SMEM_SHARED) * STAGE_BYTES >= STAGING_BYTES;
+  static constexpr int FIT = fit(SHARED_OK ? HEAD_SMEM_SHARED : HEAD_SMEM_LIMIT);
+  static constexpr int STAGES = FIT < HEAD_MAX_STAGES ? FIT : HEAD_MAX_STAGES;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + RING_BYTES + RECV_BYTES + HEAD_BAR_BYTES;  // + alignment slack
   static_assert(STAGE_BYTES % 1024 == 0 && HEAD_A_BYTES % 1024 == 0, "1024-byte aligned operand tiles");
   static_assert(BN % 32 == 0 && BN <= 256, "MMA N (and whole 32-column epilogue chunks)");
   static_assert(KS == 4 || KS == 8, "cluster size");
-  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+  static_assert(STAGES >= 2 && STAGING_BYTES <= RING_BYTES, "ring");
+  static_assert(SLOT_BYTES % 16 == 0, "bulk copy sizes");
+  static_assert(SMEM_BYTES <= HEAD_SMEM_LIMIT, "shared memory");
 };
 
 struct HeadArgs {
@@ -148,9 +169,13 @@ Q3S_DEV uint32_t cluster_rank() {
   return r;
 }
 
-Q3S_DEV void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
+// The cluster barrier in two halves: every thread of every CTA arrives, and
+// wait returns once all have.
+Q3S_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Arrival that orders no memory: for barriers that only say "this CTA got
+// this far" (the mbarrier initialisation before it is released by its own
+// fence, and a copy's completion is observed on the receiving mbarrier).
+Q3S_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 
 // The shared::cluster address of `local_saddr` in CTA `rank` of the cluster.
 Q3S_DEV uint32_t cluster_addr(uint32_t local_saddr, uint32_t rank) {
@@ -159,10 +184,20 @@ Q3S_DEV uint32_t cluster_addr(uint32_t local_saddr, uint32_t rank) {
   return remote;
 }
 
-Q3S_DEV void st_cluster_f4(uint32_t remote, float a0, float a1, float a2, float a3) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(remote), "f"(a0), "f"(a1), "f"(a2), "f"(a3)
-               : "memory");
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from this CTA's shared memory to shared::cluster address `dst` (another CTA
+// of the cluster), completing `bytes` of transactions on the mbarrier at
+// shared::cluster address `bar` (in the destination CTA).
+Q3S_DEV void bulk_s2cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "r"(src), "r"(bytes), "r"(bar)
+      : "memory");
 }
+
+// Generic-proxy shared-memory writes of this thread, ordered before later
+// async-proxy reads of them (the bulk copies above).
+Q3S_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Two fp32 values rounded to nearest-even bf16, `lo` in the low half.
 Q3S_DEV uint32_t pack_bf16x2(float lo, float hi) {
@@ -171,6 +206,9 @@ Q3S_DEV uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// Receive slot, in CTA `owner`, of the slice sent by CTA `sender` (!= owner).
+Q3S_DEV int head_slot(int sender, int owner) { return sender < owner ? sender : sender - 1; }
+
 // grid (V / BN, KS, ceil(B / HEAD_BM)), cluster (1, KS, 1)
 template <int KS, int BN>
 __global__ void __launch_bounds__(HEAD_NT, 1)
@@ -178,34 +216,51 @@ __global__ void __launch_bounds__(HEAD_NT, 1)
                      const HeadArgs a) {
   using Tile = HeadTile<KS, BN>;
   constexpr int ROWS = Tile::ROWS;
+  constexpr int STAGES = Tile::STAGES;
+  constexpr int F4_ROW = BN / 4;  // float4s per partial-tile row
   // the sampler launched after this grid as a programmatic dependent may
   // start its own preparation now; it waits for this grid before reading logits
   asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ __align__(1024) unsigned char head_smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(head_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Tile::BUF_BYTES);
-  uint64_t* empty = full + HEAD_STAGES;
-  uint64_t* done = empty + HEAD_STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  float* recv = reinterpret_cast<float*>(smem + Tile::RING_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Tile::RING_BYTES + Tile::RECV_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint64_t* recv_bar = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   int* flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int t = static_cast<int>(threadIdx.x), w = t >> 5, lane = t & 31;
   const int n0 = static_cast<int>(blockIdx.x) * BN;
   const int m0 = static_cast<int>(blockIdx.z) * HEAD_BM;
   const int kc0 = static_cast<int>(blockIdx.y) * a.kchunks;  // this CTA's first K chunk
-  const uint32_t rank = cluster_rank();
+  const int rank = static_cast<int>(cluster_rank());
 
+  auto load_chunk = [&](int kc) {
+    const int s = kc % STAGES;
+    unsigned char* st = smem + s * Tile::STAGE_BYTES;
+    mbar_expect_tx(&full[s], Tile::STAGE_BYTES);
+    const int kx = (kc0 + kc) * HEAD_BK;
+    tma_load_2d(smem_u32(st), &tm_hidden, kx, m0, &full[s]);
+    tma_load_2d(smem_u32(st + HEAD_A_BYTES), &tm_weight, kx, n0, &full[s]);
+  };
+  const int first = a.kchunks < STAGES ? a.kchunks : STAGES;  // chunks whose stage starts empty
   if (t == 0) {
-    for (int s = 0; s < HEAD_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
+    mbar_init(recv_bar, 1);
+    mbar_expect_tx(recv_bar, (KS - 1) * Tile::SLOT_BYTES);  // the only arrival; the copies complete the bytes
     *flag = 0;
     fence_mbar_init();
+    // the first loads fly while warp 1 allocates the accumulator
+    for (int kc = 0; kc < first; ++kc) load_chunk(kc);
   }
-  if (w == 0) {  // one warp allocates the accumulator's TMEM columns
+  if (w == 1) {  // the MMA warp allocates the accumulator's TMEM columns (and frees them)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(Tile::TMEM_COLS)
                  : "memory");
@@ -214,27 +269,24 @@ __global__ void __launch_bounds__(HEAD_NT, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  cluster_arrive_relaxed();  // this CTA's receive mbarrier is initialised (fenced above; waited on before the first copy)
   const uint32_t tmem = *tmem_slot;
 
   // ---- main loop: producer and MMA issuer --------------------------------
   if (t == 0) {
-    for (int kc = 0; kc < a.kchunks; ++kc) {
-      const int s = kc % HEAD_STAGES;
-      if (kc >= HEAD_STAGES && !mbar_wait_bounded(&empty[s], ((kc / HEAD_STAGES) - 1) & 1)) {
+    for (int kc = first; kc < a.kchunks; ++kc) {
+      const int s = kc % STAGES;
+      if (!mbar_wait_bounded(&empty[s], ((kc / STAGES) - 1) & 1)) {
         atomicOr(flag, 1);
         break;
       }
-      unsigned char* st = smem + s * Tile::STAGE_BYTES;
-      mbar_expect_tx(&full[s], Tile::STAGE_BYTES);
-      const int kx = (kc0 + kc) * HEAD_BK;
-      tma_load_2d(smem_u32(st), &tm_hidden, kx, m0, &full[s]);
-      tma_load_2d(smem_u32(st + HEAD_A_BYTES), &tm_weight, kx, n0, &full[s]);
+      load_chunk(kc);
     }
   } else if (t == 32) {
     constexpr uint32_t idesc = head_idesc<BN>();
     for (int kc = 0; kc < a.kchunks; ++kc) {
-      const int s = kc % HEAD_STAGES;
-      if (!mbar_wait_bounded(&full[s], (kc / HEAD_STAGES) & 1)) {
+      const int s = kc % STAGES;
+      if (!mbar_wait_bounded(&full[s], (kc / STAGES) & 1)) {
         atomicOr(flag, 1);
         break;
       }
@@ -252,77 +304,109 @@ __global__ void __launch_bounds__(HEAD_NT, 1)
   const bool finished = mbar_wait_bounded(done, 0);
   if (!finished) atomicOr(flag, 1);
   tc_fence_after();
-  tc_fence_before();
-  // every CTA of the cluster is past its MMAs: all rings are free to receive
-  cluster_sync();
-  tc_fence_after();
 
-  // ---- push: each accumulator row goes to the CTA that finishes it --------
-  // row r of the tile (TMEM lane r) belongs to CTA r / 16 of the cluster; it
-  // lands in that CTA's ring at receive slot `rank` (this CTA's K slice).  32
-  // columns at a time: TMEM -> a padded local staging chunk (each lane one
-  // row), then out with eight threads per 128-byte row segment, so every
-  // warp's remote stores cover four contiguous row segments
-  float* recv = reinterpret_cast<float*>(smem);
-  float* stg = reinterpret_cast<float*>(smem + Tile::RECV_BYTES);
+  // ---- stage and send: each warp on its own ------------------------------
+  // warp w holds TMEM lanes (tile rows) [32 w, 32 w + 32) and writes them into
+  // the staging copy of the partial tile (row-major, BN floats a row) that
+  // now occupies the idle ring; float4 column q of row r sits at q ^ (r & 7),
+  // so the eight rows of a quarter-warp's 16-byte stores hit eight different
+  // bank groups.  Rows [ROWS d, ROWS (d + 1)) then go to CTA d in one copy.
+  float* stg = reinterpret_cast<float*>(smem);
+  {
+    const int row = 32 * w + lane;
+    float4* rowp = reinterpret_cast<float4*>(stg + row * BN);
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    {
+    for (int c = 0; c < BN / 32; ++c) {
       float v[32];
       tmem_ld32(tmem + (static_cast<uint32_t>(32 * w) << 16) + static_cast<uint32_t>(32 * c), v);
-      float4* dst = reinterpret_cast<float4*>(stg + (32 * w + lane) * Tile::STG_STRIDE);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int q = 0; q < 8; ++q)
+        rowp[(8 * c + q) ^ (row & 7)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < HEAD_BM * 8 / HEAD_NT; ++i) {
-      const int f = t + HEAD_NT * i, row = f >> 3, q = f & 7;
-      const float4 p = *reinterpret_cast<const float4*>(stg + row * Tile::STG_STRIDE + 4 * q);
-      const uint32_t owner = static_cast<uint32_t>(row / ROWS);
-      const uint32_t dst = cluster_addr(
-          smem_u32(recv + (static_cast<int>(rank) * ROWS + row % ROWS) * Tile::RSTRIDE + 32 * c + 4 * q), owner);
-      st_cluster_f4(dst, p.x, p.y, p.z, p.w);
-    }
-    __syncthreads();  // the staging chunk is reused
+    fence_proxy_async_smem();
   }
   tc_fence_before();
-  cluster_sync();  // every slice has arrived
-
-  // ---- fixed-order sum of the KS K slices, rows [ROWS rank, ROWS (rank + 1)) --
-  {
-    constexpr int F4 = ROWS * BN / 4;  // float4s of the ROWS x BN slice
-    for (int f = t; f < F4; f += HEAD_NT) {
-      const int row = f / (BN / 4), c4 = f % (BN / 4);
-      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-      for (int k = 0; k < KS; ++k) {
-        const float4 p = *reinterpret_cast<const float4*>(recv + (k * ROWS + row) * Tile::RSTRIDE + 4 * c4);
-        acc.x = __fadd_rn(acc.x, p.x);
-        acc.y = __fadd_rn(acc.y, p.y);
-        acc.z = __fadd_rn(acc.z, p.z);
-        acc.w = __fadd_rn(acc.w, p.w);
-      }
-      const int grow = m0 + static_cast<int>(rank) * ROWS + row;
-      if (grow < a.B)
-        *reinterpret_cast<uint2*>(a.logits + static_cast<int64_t>(grow) * a.ldl + n0 + 4 * c4) =
-            make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
-    }
-  }
-
-  // ---- error path: wait (bounded) for this CTA's own copies and MMAs -------
-  __syncthreads();
-  if (*flag && t == 0) {
-    if (!finished) (void)mbar_wait_bounded(done, 0);
-    for (int s = 0; s < HEAD_STAGES && s < a.kchunks; ++s) (void)mbar_wait_bounded(&full[s], 0);
-    if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (w == 0) {
+  // every TMEM read is done: the accumulator can go now, unless a wait timed
+  // out (an MMA may still be running: then it goes last).  Every thread that
+  // set the flag so far sees its own write, so `clean` is one value per CTA.
+  const bool clean = __syncthreads_and(*flag == 0) != 0;
+  if (w == 1 && clean) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Tile::TMEM_COLS)
                  : "memory");
+  }
+  cluster_wait();  // every CTA's receive mbarrier is initialised
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < 32 / ROWS; ++h) {  // the owners of this warp's rows
+      const int owner = (32 * w) / ROWS + h;
+      if (owner == rank) continue;
+      const uint32_t dst = cluster_addr(
+          smem_u32(recv) + static_cast<uint32_t>(head_slot(rank, owner) * Tile::SLOT_BYTES), owner);
+      bulk_s2cluster(dst, smem_u32(stg + owner * ROWS * BN), Tile::SLOT_BYTES,
+                     cluster_addr(smem_u32(recv_bar), owner));
+    }
+  }
+
+  // ---- fixed-order sum of the KS K slices, rows [ROWS rank, ROWS (rank + 1)) --
+  bool received = true;
+  if (t == 0 && !mbar_wait_bounded(recv_bar, 0)) {
+    received = false;
+    atomicOr(flag, 1);
+  }
+  __syncthreads();  // the slices are in, and this CTA's own staging rows are written
+  cluster_arrive_relaxed();  // every copy into this CTA has landed (observed on recv_bar)
+  {
+    constexpr int PER = ROWS * F4_ROW / HEAD_NT;  // float4s of the slice per thread
+    static_assert(ROWS * F4_ROW % HEAD_NT == 0, "whole float4s per thread");
+    const float4* own = reinterpret_cast<const float4*>(stg) + rank * ROWS * F4_ROW;
+    const float4* in = reinterpret_cast<const float4*>(recv);
+    float4 acc[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) acc[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {  // fixed order: K slice 0 first
+      const float4* src = k == rank ? own : in + head_slot(k, rank) * ROWS * F4_ROW;
+      float4 p[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int f = t + HEAD_NT * i, row = f / F4_ROW, c4 = f % F4_ROW;
+        p[i] = src[row * F4_ROW + (c4 ^ (row & 7))];  // ROWS is a multiple of 8: row & 7 is the tile row's
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        acc[i].x = __fadd_rn(acc[i].x, p[i].x);
+        acc[i].y = __fadd_rn(acc[i].y, p[i].y);
+        acc[i].z = __fadd_rn(acc[i].z, p[i].z);
+        acc[i].w = __fadd_rn(acc[i].w, p[i].w);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int f = t + HEAD_NT * i, row = f / F4_ROW, c4 = f % F4_ROW;
+      const int grow = m0 + rank * ROWS + row;
+      if (grow < a.B)
+        *reinterpret_cast<uint2*>(a.logits + static_cast<int64_t>(grow) * a.ldl + n0 + 4 * c4) =
+            make_uint2(pack_bf16x2(acc[i].x, acc[i].y), pack_bf16x2(acc[i].z, acc[i].w));
+    }
+  }
+  cluster_wait();  // every copy in the cluster has landed: the staging may go
+
+  // ---- error path: wait (bounded) for this CTA's own copies and MMAs -------
+  if (*flag && t == 0) {
+    if (!finished) (void)mbar_wait_bounded(done, 0);
+    if (!received) (void)mbar_wait_bounded(recv_bar, 0);
+    for (int s = 0; s < STAGES && s < a.kchunks; ++s) (void)mbar_wait_bounded(&full[s], 0);
+    if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
+  }
+  if (!clean) {
+    tc_fence_before();
+    __syncthreads();
+    if (w == 1) {
+      tc_fence_after();
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Tile::TMEM_COLS)
+                   : "memory");
+    }
   }
 }
 
