@@ -80,6 +80,8 @@ typedef enum q3s_dtype { Q3S_DTYPE_F32 = 0, Q3S_DTYPE_BF16 = 1 } q3s_dtype;
 #define Q3S_ROW_TOPP_BOUNDARY 2   /* a top-p cumulative mass within 1e-6 of 1-p */
 #define Q3S_ROW_GREEDY 4          /* argmax path taken */
 #define Q3S_ROW_FALLBACK 8        /* u*total reached the total: last positive id taken */
+#define Q3S_ROW_EXACT_CORE 16     /* register-resident row kernel: the row was decided by the exact
+                                     whole-row core (values beyond its fast paths' proven window) */
 
 /* error_word bits (device side, OR-ed) */
 #define Q3S_DEVERR_HISTORY_ID 1        /* history id outside [0,vocab): ignored */
@@ -353,7 +355,8 @@ typedef enum {
   Q3S_POLICY_ROW_W2 = 4,
   Q3S_POLICY_ROW_W4 = 5,
   Q3S_POLICY_ROW_W8 = 6,
-  Q3S_POLICY_ROW_WMAX = 7 /* W = 12 (V > 2048) or 16 (V <= 2048) */
+  Q3S_POLICY_ROW_WMAX = 7, /* W = 12 (V > 2048) or 16 (V <= 2048) */
+  Q3S_POLICY_LEAN = 8      /* register-resident row kernel (128 threads a row) */
 } q3s_kernel_policy;
 
 /* Set the policy; returns the previous one, or -1 (unchanged) for an unknown

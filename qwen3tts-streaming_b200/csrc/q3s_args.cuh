@@ -74,6 +74,9 @@ struct CpArgs {
 // V % 8 == 0; `warps` (1, 2, 4 or 8; anything else: the widest variant,
 // 12 warps for V > 2048 and 16 below) warps per row.
 cudaError_t launch_warp_rows(const SampleArgs& a, bool bf16, cudaStream_t st, int warps);
+// Register-resident row kernels (q3s_lean.cu): icdf steps, V <= 3072,
+// V % 8 == 0, one CTA of 128 threads per row.
+cudaError_t launch_lean_rows(const SampleArgs& a, bool bf16, cudaStream_t st);
 // q3s_sample's body; `pdl` launches the sampler as a programmatic dependent
 // of the previous kernel on the stream (q3s_sampler.cu).
 q3s_status sample_impl(const q3s_sample_desc* d, cudaStream_t stream, bool pdl);

@@ -24,9 +24,10 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 CP_DIRECT, CP_ROTATE = 0, 1
 POLICY_AUTO, POLICY_CTA, POLICY_WARP = 0, 1, 2
 POLICY_ROW_W = {1: 3, 2: 4, 4: 5, 8: 6, "max": 7}
+POLICY_LEAN = 8
 PHILOX_UNIFORM, PHILOX_GUMBEL = 0, 1
 
-ROW_DRAW_BOUNDARY, ROW_TOPP_BOUNDARY, ROW_GREEDY, ROW_FALLBACK = 1, 2, 4, 8
+ROW_DRAW_BOUNDARY, ROW_TOPP_BOUNDARY, ROW_GREEDY, ROW_FALLBACK, ROW_EXACT_CORE = 1, 2, 4, 8, 16
 DEVERR_HISTORY_ID, DEVERR_OFFSETS, DEVERR_NO_MASS, DEVERR_WAIT_TIMEOUT, DEVERR_CANDIDATES = 1, 2, 4, 8, 16
 DEVERR_HISTORY_FULL = 32
 

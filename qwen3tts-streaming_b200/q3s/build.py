@@ -23,8 +23,8 @@ INCLUDE = REPO / "include"
 LIB_PATH = PKG_DIR / "libq3s_sampler.so"
 TORCH_OPS_PATH = PKG_DIR / "libq3s_torch_ops.so"
 TORCH_OPS_SRC = CSRC / "q3s_torch_ops.cpp"
-SOURCES = [CSRC / "q3s_sampler.cu", CSRC / "q3s_warp.cu", CSRC / "q3s_head.cu"]
-DEPS = SOURCES + [CSRC / "q3s_args.cuh", CSRC / "q3s_device.cuh", CSRC / "q3s_warp.cuh", CSRC / "q3s_philox.cuh", CSRC / "q3s_step.cuh", CSRC / "q3s_head.cuh",
+SOURCES = [CSRC / "q3s_sampler.cu", CSRC / "q3s_warp.cu", CSRC / "q3s_head.cu", CSRC / "q3s_lean.cu"]
+DEPS = SOURCES + [CSRC / "q3s_args.cuh", CSRC / "q3s_device.cuh", CSRC / "q3s_warp.cuh", CSRC / "q3s_philox.cuh", CSRC / "q3s_step.cuh", CSRC / "q3s_head.cuh", CSRC / "q3s_lean.cuh", CSRC / "q3s_cp.cuh", CSRC / "q3s_core.cuh",
                   INCLUDE / "q3s_sampler.h"]
 
 NVCC_FLAGS = [

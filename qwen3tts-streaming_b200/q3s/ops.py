@@ -181,10 +181,11 @@ def set_kernel_policy(policy: str) -> str:
     """Choose the kernel family for icdf steps (process-wide): "auto", "cta"
     (register-resident CTA per row), "warp" (shared-memory row kernel, warps
     per row from the batch size) or "w1" / "w2" / "w4" / "w8" / "wmax" (that
-    kernel with the warps per row forced; wmax = 12 for V > 2048, 16 below).  Returns the previous policy.  All return
-    the same ids away from flagged boundary rows."""
+    kernel with the warps per row forced; wmax = 12 for V > 2048, 16 below) or "lean" (register-resident row
+    kernel, 128 threads a row).  Returns the previous policy.  All return the same ids away from flagged boundary
+    rows."""
     codes = {"auto": _lib.POLICY_AUTO, "cta": _lib.POLICY_CTA, "warp": _lib.POLICY_WARP,
-             **{f"w{w}": c for w, c in _lib.POLICY_ROW_W.items()}}
+             **{f"w{w}": c for w, c in _lib.POLICY_ROW_W.items()}, "lean": _lib.POLICY_LEAN}
     if policy not in codes:
         raise ValueError(f"unknown kernel policy {policy!r}")
     prev = _lib.load().q3s_set_kernel_policy(codes[policy])

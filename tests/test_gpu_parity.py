@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 RTOL = 1e-5
 MAX_BOUNDARY_FRACTION = 0.02
 # the shared-memory row kernel with 1, 2, 4, 8 and 12 or 16 warps per row
-WARP_POLICIES = ["w1", "w2", "w4", "w8", "wmax"]
+WARP_POLICIES = ["w1", "w2", "w4", "w8", "wmax", "lean"]
 
 
 def _dev(x, dev):
