@@ -339,14 +339,16 @@ q3s_status q3s_head_sample(const q3s_head_desc* desc, void* stream);
 
 /* Kernel family for icdf steps that either family can serve (process-wide;
  * a tuning and test knob with no counterpart in the reference interface):
- * the register-resident CTA-per-row kernel, or the shared-memory-resident
- * row kernel with W warps per row (W chosen from the batch size, or forced).
- * AUTO picks the shared-memory kernel wherever it applies.  All return the
- * same ids, except that a draw or a top-p cut within 1e-6 of a
- * cumulative-mass edge (flagged in row_flags) may land on either side.
- * Steps that need token_counts, col_shift, processed_logits or counts_out,
- * Gumbel mode, or a vocabulary outside (1024, 3072] or not a multiple of 8
- * always take CTA-per-row. */
+ * the register-resident CTA-per-row kernel, the shared-memory-resident row
+ * kernel with W warps per row (W chosen from the batch size, or forced), or
+ * the register-resident row kernel that resolves each row exactly on a short
+ * list (LEAN, 128 threads a row).  AUTO takes LEAN for batches of more than
+ * two rows per SM and the shared-memory kernel below that, wherever they
+ * apply.  All return the same ids, except that a draw or a top-p cut within
+ * 1e-6 of a cumulative-mass edge (flagged in row_flags) may land on either
+ * side.  Steps that need token_counts, col_shift or counts_out, Gumbel mode,
+ * or a vocabulary not a multiple of 8 always take CTA-per-row; the
+ * shared-memory kernel also needs 1024 < V <= 3072, LEAN V <= 3072. */
 typedef enum {
   Q3S_POLICY_AUTO = 0,
   Q3S_POLICY_CTA = 1,

@@ -48,6 +48,8 @@
 // MinNewTokensLengthLogitsProcessor's EOS gate).
 #pragma once
 
+#include <type_traits>
+
 #include "q3s_core.cuh"
 
 namespace q3s {
@@ -97,6 +99,14 @@ Q3S_DEV float div_rn_row(float x, float d, float r) {
   return __fmaf_rn(__fmaf_rn(-q1, d, x), r, q1);
 }
 
+// div_rn_row on the two lanes of packed fp32x2 arithmetic (the same roundings).
+Q3S_DEV float2 div2_rn_row(float2 x, float d, float r) {
+  const float2 dd = make_float2(-d, -d), rr = make_float2(r, r);
+  const float2 q0 = __fmul2_rn(x, rr);
+  const float2 q1 = __ffma2_rn(__ffma2_rn(q0, dd, x), rr, q0);
+  return __ffma2_rn(__ffma2_rn(q1, dd, x), rr, q1);
+}
+
 // Integer bin of a value below a reference: RN(c0 - c v) - 2^23 as the
 // float's bits, clamped to 255, with c0 = RN(c ref + 2^23 + 1).  One fused
 // multiply-add rounds once, so the bin is a monotone non-increasing function
@@ -107,10 +117,10 @@ Q3S_DEV uint32_t ref_bin(float v, float c, float c0) {
 }
 Q3S_DEV float ref_c0(float c, float ref) { return __fadd_rn(__fmul_rn(c, ref), 8388609.0f); }
 
-// Bin of a softmax weight w in [0, 1]: 16 bins per octave by the exponent and
+// Bin of a softmax weight w in [0, 1 + 2^-23]: 16 bins per octave by the exponent and
 // the top 4 mantissa bits (bin 0: w in [1, 1 + 1/16)), 255 for w < 2^-15.9
 // and w = 0.  Monotone non-increasing in w.
-Q3S_DEV uint32_t wbin(float w) { return static_cast<uint32_t>(min(max(2032 - static_cast<int>(__float_as_uint(w) >> 19), 0), 255)); }
+Q3S_DEV uint32_t wbin(float w) { return min(2032u - (__float_as_uint(w) >> 19), 255u); }
 // The midpoint weight of a wbin bin (an estimate of each entry's weight).
 Q3S_DEV float wbin_mid(uint32_t k) { return __uint_as_float(((2032u - k) << 19) | (1u << 18)); }
 
@@ -501,6 +511,7 @@ __global__ void __launch_bounds__(NT, lean::min_blocks(NT)) sample_lean_kernel(c
   __shared__ uint32_t maxkey;  // largest exact key on the list
   __shared__ int top_above;    // whole-vocabulary rows: bit 0 / 1 -- the cut clears the bracket's lower / upper guard
   __shared__ int brk[4];       // whole-vocabulary rows: the bracket (lo, hi bins), entries above it, usable
+  __shared__ uint8_t dummy_byte;  // the history scatter's target for ids outside [0, V)
   const int t = static_cast<int>(threadIdx.x);
   const int b = static_cast<int>(blockIdx.x);
   const int v0 = t * E;
@@ -576,12 +587,12 @@ __global__ void __launch_bounds__(NT, lean::min_blocks(NT)) sample_lean_kernel(c
       mid0 = min(o1, (o0 + 3) & ~3);
       mid1 = mid0 + ((o1 - mid0) & ~3);
     }
+    // branch-free: an id outside [0, V) is stored to a dummy byte and reported
     bool bad = false;
     auto put = [&](int idv) {
-      if (static_cast<unsigned>(idv) < static_cast<unsigned>(V))
-        sh.seen[idv] = 1;
-      else
-        bad = true;
+      const bool ok = static_cast<unsigned>(idv) < static_cast<unsigned>(V);
+      bad |= !ok;
+      *(ok ? &sh.seen[idv] : &dummy_byte) = 1;
     };
     const int nv = (mid1 - mid0) >> 2;
     const int4* hv = reinterpret_cast<const int4*>(h + mid0);
@@ -660,18 +671,36 @@ __global__ void __launch_bounds__(NT, lean::min_blocks(NT)) sample_lean_kernel(c
       }
     }
   } else {
+    // branch-free: both penalty branches for every entry, two entries per
+    // packed fp32x2 operation; the temperature division in its own variant
+    auto vocab_pass = [&](auto divt_tag) {
+      constexpr bool DIVT = decltype(divt_tag)::value;
 #pragma unroll
-    for (int c = 0; c < E / 8; ++c) {
+      for (int c = 0; c < E / 8; ++c) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int j = 8 * c + i;
-        float y = byte_set(supb[c], i) ? NEG_SUPPRESS : x[j];
-        if (byte_set(prw[c], i)) y = y > 0.0f ? div_rn_row(y, pen, rpen) : __fmul_rn(y, pen);
-        if (divT) y = y == -INFINITY ? y : div_rn_row(y, T, rT);
-        x[j] = y;
-        m = max_nan(m, y);
+        for (int i = 0; i < 8; i += 2) {
+          const int j = 8 * c + i;
+          float y0 = byte_set(supb[c], i) ? NEG_SUPPRESS : x[j];
+          float y1 = byte_set(supb[c], i + 1) ? NEG_SUPPRESS : x[j + 1];
+          const float2 q = div2_rn_row(make_float2(y0, y1), pen, rpen);
+          const float2 py = __fmul2_rn(make_float2(y0, y1), make_float2(pen, pen));
+          if (byte_set(prw[c], i)) y0 = y0 > 0.0f ? q.x : py.x;
+          if (byte_set(prw[c], i + 1)) y1 = y1 > 0.0f ? q.y : py.y;
+          if constexpr (DIVT) {
+            const float2 st = div2_rn_row(make_float2(y0, y1), T, rT);
+            y0 = y0 == -INFINITY ? y0 : st.x;
+            y1 = y1 == -INFINITY ? y1 : st.y;
+          }
+          x[j] = y0;
+          x[j + 1] = y1;
+          m = max_nan(m, max_nan(y0, y1));
+        }
       }
-    }
+    };
+    if (divT)
+      vocab_pass(std::true_type{});
+    else
+      vocab_pass(std::false_type{});
   }
   m = block_max_nan<NT, E>(m, sh, rb);
   // the fast paths' window: finite values within +-2000, penalty and
@@ -707,7 +736,10 @@ __global__ void __launch_bounds__(NT, lean::min_blocks(NT)) sample_lean_kernel(c
     // pass 2: distance bins 1/8 wide below the maximum (bin 255: the rest)
     const float c0 = ref_c0(8.0f, m);
 #pragma unroll
-    for (int j = 0; j < E; ++j) atomicAdd(&sh.hist[0][ref_bin(x[j], 8.0f, c0)], 1u);
+    for (int j = 0; j < E; ++j) {
+      const uint32_t k = ref_bin(x[j], 8.0f, c0);
+      if (k < 255u) atomicAdd(&sh.hist[0][k], 1u);  // bin 255 (the rest) is never read
+    }
     __syncthreads();
     uint32_t kb, nthru;
     warp_bin_of_rank(sh.hist[0], static_cast<uint32_t>(K), kb, nthru);  // every warp, same answer
@@ -839,25 +871,34 @@ __global__ void __launch_bounds__(NT, lean::min_blocks(NT)) sample_lean_kernel(c
     // weight's bits
     const float mL = __fmul_rn(m, LOG2E);
     float2 zs = make_float2(0.0f, 0.0f);
+    auto weights_pass = [&](auto cut_tag) {
+      constexpr bool CUT = decltype(cut_tag)::value;
 #pragma unroll
-    for (int j = 0; j < E; j += 2) {
-      const float2 arg = __ffma2_rn(make_float2(x[j], x[j + 1]), make_float2(LOG2E, LOG2E), make_float2(-mL, -mL));
-      const float w0 = ex2(arg.x), w1 = ex2(arg.y);
-      x[j] = w0;
-      x[j + 1] = w1;
-      zs = __fadd2_rn(zs, make_float2(w0, w1));
-      if (cut) {
-        atomicAdd(&sh.hist[0][wbin(w0)], 1u);
-        atomicAdd(&sh.hist[0][wbin(w1)], 1u);
+      for (int j = 0; j < E; j += 2) {
+        const float2 arg = __ffma2_rn(make_float2(x[j], x[j + 1]), make_float2(LOG2E, LOG2E), make_float2(-mL, -mL));
+        const float w0 = ex2(arg.x), w1 = ex2(arg.y);
+        x[j] = w0;
+        x[j + 1] = w1;
+        zs = __fadd2_rn(zs, make_float2(w0, w1));
+        if constexpr (CUT) {
+          // bin 255 (weights < 2^-15.9 and zeros) is not counted
+          const uint32_t k0 = wbin(w0), k1 = wbin(w1);
+          if (k0 < 255u) atomicAdd(&sh.hist[0][k0], 1u);
+          if (k1 < 255u) atomicAdd(&sh.hist[0][k1], 1u);
+        }
       }
-    }
+    };
+    if (cut)
+      weights_pass(std::true_type{});
+    else
+      weights_pass(std::false_type{});
     float loc = __fadd_rn(zs.x, zs.y);  // this thread's kept weight (the draw's per-thread total)
     const float Z = block_sum_f<NT, E>(loc, sh, rb);  // also publishes the histogram
     bool ok = true;
     if (cut) {
-      // warp 0: estimated ascending masses (count x bin midpoint; the last
-      // bin, weights < 2^-15.9 and zeros, at 2^-17 each), the bin where they
-      // pass tau, a 5-bin bracket around it
+      // warp 0: estimated ascending masses (count x bin midpoint; weights
+      // < 2^-15.9 are not counted), the bin where they pass tau, a 5-bin
+      // bracket around it
       const float frac = __fsub_rn(1.0f, top_p);
       const float tau = __fmul_rn(frac, Z);
       if (t < 32) {
@@ -868,7 +909,7 @@ __global__ void __launch_bounds__(NT, lean::min_blocks(NT)) sample_lean_kernel(c
 #pragma unroll
         for (int i = 7; i >= 0; --i) {
           const uint32_t k = static_cast<uint32_t>(8 * lane + i);
-          run = __fadd_rn(run, __fmul_rn(static_cast<float>(c[i]), k < 255u ? wbin_mid(k) : 0x1p-17f));
+          run = __fadd_rn(run, __fmul_rn(static_cast<float>(c[i]), wbin_mid(k)));  // bin 255 holds no counts
           sl[i] = run;
         }
         float inc = run;

@@ -716,7 +716,11 @@ q3s_status sample_impl(const q3s_sample_desc* d, cudaStream_t stream, bool pdl) 
   // any vocabulary up to 3072 that is a multiple of 8
   const bool lean_ok = a.mode == Q3S_DRAW_ICDF && !a.token_counts && !a.col_shift && !a.counts_out &&
                        V % 8 == 0 && V <= 3072 && (!a.suppress || a.vec_suppress);
-  if (lean_ok && policy == Q3S_POLICY_LEAN) {
+  // AUTO: the register-resident kernel beyond two rows per SM, where it is
+  // the fastest measured (B200, configs 3 and 4); the shared-memory row
+  // kernel below that (latency-bound batches)
+  const bool lean_auto = policy == Q3S_POLICY_AUTO && a.B > 2 * device_sm_count();
+  if (lean_ok && (policy == Q3S_POLICY_LEAN || lean_auto)) {
     const cudaError_t e = q3s::launch_lean_rows(a, bf16, st);
     if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample lean launch failed: %s", cudaGetErrorString(e));
     return ok();
