@@ -36,7 +36,7 @@
 
 namespace q3s {
 
-constexpr int MAX_NBUF = 8;
+constexpr int MAX_NBUF = 16;
 
 // ---------------------------------------------------------------------------
 // one sampling step, one CTA per row
@@ -818,8 +818,10 @@ q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
   a.row_bytes = static_cast<uint32_t>(V * esz);
   a.bulk = aligned16(d->logits) && (a.row_bytes % 16 == 0) && ((d->logits_row_stride * esz) % 16 == 0) &&
            ((d->logits_stage_stride * esz) % 16 == 0);
-  // ring of stage rows in flight: ~16 KB (4 x 4 KB rows at V=2048 bf16), 2..8 slots
-  a.nbuf = a.bulk ? std::max(2, std::min(q3s::MAX_NBUF, static_cast<int>((16u * 1024u) / a.row_bytes))) : 0;
+  // ring of stage rows in flight: up to 64 KB, 2..16 slots -- a whole
+  // 15-stage frame of 4 KB rows (V = 2048 bf16), so that every stage row of
+  // a CTA's first row is requested at once and later stages never wait
+  a.nbuf = a.bulk ? std::max(2, std::min(q3s::MAX_NBUF, static_cast<int>((64u * 1024u) / a.row_bytes))) : 0;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Gumbel frames (the engine graph's stages) with rows of at most 2048
@@ -830,6 +832,25 @@ q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
       policy != Q3S_POLICY_CTA) {
     const size_t dyn = static_cast<size_t>(a.nbuf) * a.row_bytes;
     auto kern = bf16 ? q3s::cp_fast_kernel<true> : q3s::cp_fast_kernel<false>;
+    {
+      // the ring may pass the 48 KB default: opt in (idempotent per kernel
+      // and device; the value only ever grows)
+      static std::atomic<int> granted[2][64];
+      int dev = 0;
+      cudaGetDevice(&dev);
+      const bool known = dev >= 0 && dev < 64;
+      if (!known || granted[bf16][dev].load(std::memory_order_acquire) < static_cast<int>(dyn)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
+        if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample_cp_frame smem attribute: %s", cudaGetErrorString(e));
+        if (known) {
+          int cur = granted[bf16][dev].load(std::memory_order_relaxed);
+          while (cur < static_cast<int>(dyn) &&
+                 !granted[bf16][dev].compare_exchange_weak(cur, static_cast<int>(dyn), std::memory_order_release)) {
+          }
+        }
+      }
+    }
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, q3s::CPF_NT, dyn) != cudaSuccess || per_sm <= 0)
       per_sm = 1;
