@@ -695,7 +695,7 @@ def test_philox_seeds_match_host_generator(cuda_device, q3s_lib):
 # capacity layout of the history (RowHistory): the same ids as packed
 # ---------------------------------------------------------------------------
 
-@pytest.mark.parametrize("policy", ["auto", "cta", "w4", "wmax"])
+@pytest.mark.parametrize("policy", ["auto", "cta", "w4", "wmax", "lean"])
 @pytest.mark.parametrize("cfg", [1, 3])
 def test_capacity_layout_matches_packed_and_oracle(cuda_device, q3s_lib, oracle_configs, cfg, policy):
     """Rows in regions with spare capacity: ids, flags and processed logits
@@ -750,3 +750,37 @@ def test_capacity_layout_bad_length_is_reported(cuda_device, q3s_lib):
             plan.launch()
         torch.cuda.synchronize()
         assert int(err.item()) & _lib.DEVERR_OFFSETS, policy
+
+
+# ---------------------------------------------------------------------------
+# the lean kernel's fast paths and its exact core
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("cfg", [1, 3, 4])
+def test_lean_fast_paths_decide_benchmark_rows(cuda_device, q3s_lib, oracle_configs, cfg):
+    """Every row of the benchmark configurations is decided on the lean
+    kernel's fast paths (no Q3S_ROW_EXACT_CORE flag), with the oracle's ids."""
+    b, ref = oracle_configs(cfg)
+    g, kw = _packed_args(b, cuda_device)
+    ids, kf, err = _run_policy("lean", g, kw, cuda_device)
+    assert err == 0
+    assert not np.any(kf & _lib.ROW_EXACT_CORE), f"config {cfg}: rows {np.nonzero(kf & _lib.ROW_EXACT_CORE)[0][:8]}"
+    assert_ids_match(ids, ref, kf, f"lean config {cfg}", max_frac=MAX_BOUNDARY_FRACTION)
+
+
+def test_lean_rows_outside_the_window_take_the_exact_core(cuda_device, q3s_lib):
+    """Rows the fast paths cannot prove exact -- a logit beyond +-2000, a
+    top-k beyond the candidate path's 128, a 600-way tie that overflows the
+    list -- are flagged Q3S_ROW_EXACT_CORE and still match the oracle; an
+    ordinary row beside them is not flagged."""
+    rng = np.random.default_rng(31)
+    x = (rng.standard_normal((4, 3072)) * 3).astype(np.float32)
+    x[0, 17] = 5000.0        # beyond the fast window
+    x[2, :600] = 50.0        # a 600-way tie at the top (list overflow for k = 50)
+    T = np.full(4, 0.9, np.float32)
+    for k, p, exact_rows in ((50, 0.9, (0, 2)), (300, 0.9, (0, 1, 2, 3))):
+        ids, kf, err, ref = _warp_case(cuda_device, x, policy="lean", T=T, k=k, p=p)
+        assert err == 0
+        assert_ids_match(ids, ref, kf, f"lean exact core k={k}")
+        flagged = set(np.nonzero(kf & _lib.ROW_EXACT_CORE)[0].tolist())
+        assert flagged == set(exact_rows), f"k={k}: exact-core rows {sorted(flagged)}"
