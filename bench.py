@@ -897,7 +897,14 @@ def run_q3s(args):
     achieved = bytes_step / (ms_step / 1000) / 1e9
     traffic = profile_traffic("sample_smem_cfg1_ncu.txt")
     clk = clocks.summary(t0, t1)
-    ok = bool(same and e2e_ok and check is not None and check["unexplained_mismatches"] == 0 and err_word == 0)
+    # every rank checks its own launches; rank 0 also holds the oracle's
+    # verdict on the gathered batch; all ranks agree on the outcome (MIN)
+    ok = bool(same and e2e_ok and err_word == 0 and
+              (rank != 0 or (check is not None and check["unexplained_mismatches"] == 0)))
+    if world > 1:
+        okt = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+        ok = bool(okt.item())
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(total / (ms_step / 1000), 1), "unit": "tokens/s",
