@@ -78,6 +78,8 @@ def parse_args():
                          "prints no bench value")
     ap.add_argument("--profile-step", action="store_true",
                     help="with --profile-config 1 or 4: the launches are q3s_step_update over that config's history")
+    ap.add_argument("--profile-head", action="store_true",
+                    help="with --profile-config 1: the codec head GEMM alone (hidden [B,2048] x W^T, V=3072)")
     ap.add_argument("--profile-gumbel", action="store_true",
                     help="with --profile-config 1: the engine layout (gumbel, token_counts, in-place counts)")
     return ap.parse_args()
@@ -1028,6 +1030,12 @@ def run_profile(args):
         guard = q3s.StepGuard(b.B, device=dev)
         ids = torch.from_numpy(rng.integers(0, 2048, b.B)).to(dev)
         plans = [_StepPlan(guard, ids, b.history if i == 0 else b.history.clone(), b.offsets) for i in range(4)]
+    elif args.profile_head:
+        b = workloads.make_batch(cfg)
+        g = torch.Generator().manual_seed(2024)
+        hidden = torch.randn(b.B, HEAD_H, generator=g).to(torch.bfloat16).to(dev)
+        weight = (torch.randn(b.V, HEAD_H, generator=g) * (3.0 / HEAD_H ** 0.5)).to(torch.bfloat16).to(dev)
+        plans = [q3s.HeadPlan(hidden, weight.clone() if i else weight) for i in range(4)]
     elif cfg == 2:
         f = workloads.make_cp_frame().to(dev)
         plans = [q3s.CpFramePlan(f.base if i == 0 else f.base.clone(), mode="gumbel", topk=50,
@@ -1046,6 +1054,7 @@ def run_profile(args):
         plans[i % len(plans)].launch(stream)
     torch.cuda.synchronize()
     print(json.dumps({"profile": True, "config": cfg, "step_update": bool(args.profile_step),
+                      "head": bool(args.profile_head),
                       "gumbel": bool(args.profile_gumbel), "launches": n}), flush=True)
 
 
