@@ -59,12 +59,19 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
     bulk_g2s(cpf_ring + static_cast<size_t>(slot) * a.row_bytes, src, a.row_bytes, &bars[slot]);
   };
   // noise of item g (row i, stage j) by rank into half (g & 1) of sh.noise
-  auto load_noise = [&](int g) {
-    if (g >= nitems || t >= K) return;
+  // noise of item g (row i, stage j), entry t of its K, from global memory
+  // (0 past the end): fetched into a register at a stage's start and stored
+  // at its end, so the load's latency overlaps the stage instead of holding
+  // the fetching warps (and with them the stage's first barrier)
+  auto fetch_noise = [&](int g) -> float {
+    if (g >= nitems || t >= K) return 0.0f;
     const int i = g / S, j = g % S;
     const int b = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
-    sh.noise[(g & 1) * CPF_CAP + t] =
-        __ldg(a.noise + static_cast<int64_t>(b) * a.noise_row_stride + static_cast<int64_t>(j) * a.noise_stage_stride + t);
+    return __ldg(a.noise + static_cast<int64_t>(b) * a.noise_row_stride + static_cast<int64_t>(j) * a.noise_stage_stride + t);
+  };
+  // ... into half (g & 1) of sh.noise (by rank)
+  auto stash_noise = [&](int g, float nz) {
+    if (g < nitems && t < K) sh.noise[(g & 1) * CPF_CAP + t] = nz;
   };
 
   clear_hist<NT, E>(sh);
@@ -72,7 +79,7 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
     for (int s = 0; s < a.nbuf; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
-  load_noise(0);
+  stash_noise(0, fetch_noise(0));
   __syncthreads();
   if (t == 0)
     for (int g = 0; g < min(a.nbuf, nitems); ++g) issue(g);
@@ -98,7 +105,7 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
       // every thread is past the previous stage: refill its slot, prefetch
       // the next stage's noise
       if (t == 0 && g > 0 && g - 1 + a.nbuf < nitems) issue(g - 1 + a.nbuf);
-      load_noise(g + 1);
+      const float nz_next = fetch_noise(g + 1);
       const unsigned char* row = cpf_ring + static_cast<size_t>(slot) * a.row_bytes;
       float x[E];
       uint32_t vmask = 0;
@@ -189,10 +196,10 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
           if (a.row_flags) a.row_flags[static_cast<int64_t>(b) * S + j] = flags;
         }
         prev = id;
-        // the core loads its own noise into sh.noise[0, K): load the next
-        // stage's again once every thread is done with the core
+        // the core loads its own noise into sh.noise[0, K): store the next
+        // stage's once every thread is done with the core
         __syncthreads();
-        load_noise(g + 1);
+        stash_noise(g + 1, nz_next);
         continue;
       }
       // 3. candidates (bins 0..bK) in index order
@@ -279,6 +286,7 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
         if (a.row_flags) a.row_flags[static_cast<int64_t>(b) * S + j] = 0;
       }
       prev = id;
+      stash_noise(g + 1, nz_next);  // half (g + 1) & 1: last read in the previous stage
     }
   }
 }
