@@ -1,7 +1,7 @@
 // q3s_cp.cuh -- code-predictor frame for the engine graph's stage sampler
 // (CodePredictorUnrolled._select_token, scripts/export/utils.py:1178-1193,
 // looped at :1218-1237) in Gumbel mode: one CTA of 256 threads per row runs
-// all S stages, each a short fixed chain of seven barriers.
+// all S stages, each a short fixed chain of five barriers.
 //
 // A frame is latency-bound (one row per SM at the engine's batch sizes), so
 // a stage does only what exactly-K top-k + Gumbel needs, with thread t
@@ -11,13 +11,14 @@
 //   2. one histogram of d = max - v in bins 1/8 wide over d < 32 (shared
 //      atomics; floor((max - v) * 8) is monotone in v, so every entry at or
 //      above the K-th largest lies in the bin holding it or an earlier one);
-//      warp 0 finds that bin and clears what it read;
-//   3. those entries compacted in index order (per-warp ballot counts, one
-//      exchange) -- at most 256 of them, one per thread;
-//   4. each candidate's exact rank (value desc, index asc) by all pairs, up
-//      to 4 threads per candidate; the first K score v / T + noise[rank] (the
-//      noise of this stage was loaded during the previous one); the argmax
-//      (lowest rank on ties).
+//      warp 0 finds that bin and turns the counts into exclusive prefixes;
+//   3. those entries placed by bin (a counting sort: each takes its bin's
+//      cursor, advanced atomically), so every bin is a contiguous range;
+//   4. each candidate's exact rank (value desc, index asc) = its bin's start
+//      plus its rank among the few entries of its own bin (bins are monotone
+//      in the value and equal values share a bin); the first K score v / T +
+//      noise[rank] (the noise of this stage was fetched during the previous
+//      one); the argmax (lowest rank on ties).
 // Rows outside that pattern -- the K-th largest 32 or more below the maximum,
 // more than 256 entries down to its bin (massive ties) -- take the general
 // CTA sampler core, which holds the row in the same register layout.
@@ -38,7 +39,7 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
   __shared__ Scratch<NT, E> sh;
   __shared__ __align__(8) uint64_t bars[MAX_NBUF];
   __shared__ float wmax[NW], wbs[NW];
-  __shared__ int wcnt[NW], wbr[NW], wbi[NW];
+  __shared__ int wbr[NW], wbi[NW];
   __shared__ int sel[2];
   extern __shared__ __align__(128) unsigned char cpf_ring[];
   const int t = static_cast<int>(threadIdx.x), w = t >> 5, lane = t & 31;
@@ -132,18 +133,21 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
       m = wmax[0];
 #pragma unroll
       for (int k = 1; k < NW; ++k) m = fmaxf(m, wmax[k]);
-      // 2. histogram of floor((m - v) * 8) over d < 32
+      // 2. histogram of floor((m - v) * 8) over d < 32 (each entry's bin
+      //    kept; 256 = beyond)
+      int eb[E];
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         const float ev = __fmul_rn(__fsub_rn(m, x[e]), 8.0f);
-        if (ev < 256.0f) atomicAdd(&sh.hist[0][static_cast<uint32_t>(ev)], 1u);
+        eb[e] = ev < 256.0f ? static_cast<int>(ev) : 256;
+        if (eb[e] < 256) atomicAdd(&sh.hist[0][eb[e]], 1u);
       }
       __syncthreads();  // (2)
       if (w == 0) {
+        // the bin holding the K-th largest and the count through it; every
+        // bin's count becomes its exclusive prefix (the placement cursor)
         uint4* hb = reinterpret_cast<uint4*>(sh.hist[0]) + 2 * lane;
         const uint4 h0 = hb[0], h1 = hb[1];
-        hb[0] = make_uint4(0, 0, 0, 0);  // the histogram's zero invariant
-        hb[1] = make_uint4(0, 0, 0, 0);
         const uint32_t c[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
         uint32_t sum = 0;
 #pragma unroll
@@ -154,6 +158,15 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
           const uint32_t y = __shfl_up_sync(FULL, inc, o);
           if (lane >= o) inc += y;
         }
+        uint32_t pre[8];
+        uint32_t run = inc - sum;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          pre[k] = run;
+          run += c[k];
+        }
+        hb[0] = make_uint4(pre[0], pre[1], pre[2], pre[3]);
+        hb[1] = make_uint4(pre[4], pre[5], pre[6], pre[7]);
         const uint32_t kk = static_cast<uint32_t>(K);
         const unsigned hit = __ballot_sync(FULL, inc >= kk && inc - sum < kk);
         if (lane == 0) {
@@ -178,7 +191,10 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
       const int bK = sel[0], n = sel[1];
       int id, flags = 0;
       if (bK >= 256 || n > CPF_CAP) {
-        // outside the fast pattern: the general CTA core on the same registers
+        // outside the fast pattern: the general CTA core on the same
+        // registers, the histogram (now cursors) back to zero first
+        for (int i = t; i < NBINS; i += NT) sh.hist[0][i] = 0u;
+        __syncthreads();
         RowCfg c;
         c.mode = Q3S_DRAW_GUMBEL;
         c.greedy = false;
@@ -202,57 +218,38 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
         stash_noise(g + 1, nz_next);
         continue;
       }
-      // 3. candidates (bins 0..bK) in index order
-      uint32_t cm = 0;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float ev = __fmul_rn(__fsub_rn(m, x[e]), 8.0f);
-        cm |= ((v0 + e < V && ev < static_cast<float>(bK + 1)) ? 1u : 0u) << e;
-      }
-      const uint32_t cnt = __popc(cm);
-      uint32_t incl = cnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(FULL, incl, o);
-        if (lane >= o) incl += y;
-      }
-      if (lane == 31) wcnt[w] = static_cast<int>(incl);
-      __syncthreads();  // (4)
-      int p = static_cast<int>(incl - cnt);
-      for (int k = 0; k < w; ++k) p += wcnt[k];
+      // 3. the candidates (bins 0..bK) placed by bin (a counting sort: slot =
+      //    the bin's cursor, advanced atomically), so each bin is a
+      //    contiguous range of the list
 #pragma unroll
       for (int e = 0; e < E; ++e)
-        if ((cm >> e) & 1u) {
-          sh.xs[p] = x[e];
-          sh.cand[p].y = static_cast<uint32_t>(v0 + e);
-          ++p;
+        if (eb[e] <= bK) {
+          const uint32_t slot = atomicAdd(&sh.hist[0][eb[e]], 1u);
+          sh.xs[slot] = x[e];
+          sh.cand[slot] = make_uint4(0u, static_cast<uint32_t>(v0 + e), static_cast<uint32_t>(eb[e]), 0u);
         }
-      __syncthreads();  // (5)
-      // 4. ranks (LP threads per candidate, each counting over every LP-th
-      //    group of four), scores, argmax (lowest rank on ties)
+      __syncthreads();  // (4)
+      // 4. exact rank (value desc, index asc): the bins are monotone in the
+      //    value and equal values share a bin, so the rank is the bin's start
+      //    plus the rank inside the bin; the first K score v / T +
+      //    noise[rank]; the argmax (lowest rank on ties).  A bin's cursor now
+      //    holds the next bin's start.
       float bs = -INFINITY;
       int br = 0x7fffffff, bi = 0;
-      {
-        const int LP = n <= 64 ? 4 : (n <= 128 ? 2 : 1);
-        const int p = t / LP, sub = t % LP;
-        const bool act = p < n;
-        const float vp = act ? sh.xs[p] : 0.0f;
-        const int n4 = (n + 3) >> 2;
-        int r = 0;
-        if (act)
-          for (int q4 = sub; q4 < n4; q4 += LP) {
-            const float4 f = reinterpret_cast<const float4*>(sh.xs)[q4];
-            const int q = 4 * q4;
-            r += (q < n) && ((f.x > vp) || (f.x == vp && q < p));
-            r += (q + 1 < n) && ((f.y > vp) || (f.y == vp && q + 1 < p));
-            r += (q + 2 < n) && ((f.z > vp) || (f.z == vp && q + 2 < p));
-            r += (q + 3 < n) && ((f.w > vp) || (f.w == vp && q + 3 < p));
-          }
-        for (int o = 1; o < LP; o <<= 1) r += __shfl_xor_sync(FULL, r, o);
-        if (act && sub == 0 && r < K) {
+      if (t < n) {
+        const float vp = sh.xs[t];
+        const uint4 me = sh.cand[t];
+        const uint32_t k = me.z;
+        const uint32_t start = k ? sh.hist[0][k - 1] : 0u, end = sh.hist[0][k];
+        int r = static_cast<int>(start);
+        for (uint32_t q = start; q < end; ++q) {
+          const float f = sh.xs[q];
+          r += (f > vp) || (f == vp && sh.cand[q].y < me.y);
+        }
+        if (r < K) {
           bs = __fadd_rn(__fdiv_rn(vp, T), sh.noise[(g & 1) * CPF_CAP + r]);
           br = r;
-          bi = static_cast<int>(sh.cand[p].y);
+          bi = static_cast<int>(me.y);
         }
       }
 #pragma unroll
@@ -270,7 +267,8 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
         wbr[w] = br;
         wbi[w] = bi;
       }
-      __syncthreads();  // (6)
+      __syncthreads();  // (5)
+      for (int i = t; i < NBINS; i += NT) sh.hist[0][i] = 0u;  // the zero invariant, for the next stage
       bs = wbs[0];
       br = wbr[0];
       id = wbi[0];
