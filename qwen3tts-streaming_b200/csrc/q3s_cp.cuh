@@ -252,33 +252,32 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
           bi = static_cast<int>(me.y);
         }
       }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const float os = __shfl_xor_sync(FULL, bs, o);
-        const int orr = __shfl_xor_sync(FULL, br, o), oi = __shfl_xor_sync(FULL, bi, o);
-        if (os > bs || (os == bs && orr < br)) {
-          bs = os;
-          br = orr;
-          bi = oi;
-        }
-      }
+      // argmax (score desc, rank asc) by two warp reductions: the largest
+      // order-preserving score key, then the lowest rank among the lanes
+      // holding it (ranks are distinct); lanes without a score hold key 0
+      auto warp_best = [&](uint32_t key, uint32_t rank, int idv, uint32_t& bkey, uint32_t& brank, int& bid) {
+        bkey = __reduce_max_sync(FULL, key);
+        brank = __reduce_min_sync(FULL, key == bkey ? rank : 0xffffffffu);
+        const unsigned hit = __ballot_sync(FULL, key == bkey && rank == brank);
+        bid = __shfl_sync(FULL, idv, hit ? __ffs(hit) - 1 : 0);
+      };
+      uint32_t wk, wr;
+      int wi;
+      warp_best(br != 0x7fffffff ? f2key(bs) : 0u, static_cast<uint32_t>(br), bi, wk, wr, wi);
       if (lane == 0) {
-        wbs[w] = bs;
-        wbr[w] = br;
-        wbi[w] = bi;
+        wbs[w] = __uint_as_float(wk);  // the key's bits
+        wbr[w] = static_cast<int>(wr);
+        wbi[w] = wi;
       }
       __syncthreads();  // (5)
       for (int i = t; i < NBINS; i += NT) sh.hist[0][i] = 0u;  // the zero invariant, for the next stage
-      bs = wbs[0];
-      br = wbr[0];
-      id = wbi[0];
-#pragma unroll
-      for (int k = 1; k < NW; ++k)
-        if (wbs[k] > bs || (wbs[k] == bs && wbr[k] < br)) {
-          bs = wbs[k];
-          br = wbr[k];
-          id = wbi[k];
-        }
+      {
+        // the same reduction over the warps' results (lanes 0..NW-1)
+        const bool in = lane < NW;
+        uint32_t fk, fr;
+        warp_best(in ? __float_as_uint(wbs[lane]) : 0u, in ? static_cast<uint32_t>(wbr[lane]) : 0xffffffffu,
+                  in ? wbi[lane] : 0, fk, fr, id);
+      }
       if (t == 0) {
         a.ids_out[static_cast<int64_t>(b) * S + j] = id;
         if (a.row_flags) a.row_flags[static_cast<int64_t>(b) * S + j] = 0;
