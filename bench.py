@@ -77,7 +77,10 @@ def parse_args():
                     help="plain eager launches of one config (0-4; 2 = code-predictor frame) for ncu; "
                          "prints no bench value")
     ap.add_argument("--profile-step", action="store_true",
-                    help="with --profile-config 1 or 4: the launches are q3s_step_update over that config's history")
+                    help="with --profile-config 1 or 4: the launches are q3s_step_update appending in place "
+                         "into that config's history (capacity layout)")
+    ap.add_argument("--profile-packed", action="store_true",
+                    help="with --profile-step: the packed layout instead (every row copied with its new id)")
     ap.add_argument("--profile-head", action="store_true",
                     help="with --profile-config 1: the codec head GEMM alone (hidden [B,2048] x W^T, V=3072)")
     ap.add_argument("--profile-gumbel", action="store_true",
@@ -1027,9 +1030,17 @@ def run_profile(args):
 
         b = workloads.make_batch(cfg).to(dev)
         rng = np.random.default_rng(4242 + cfg)
-        guard = q3s.StepGuard(b.B, device=dev)
         ids = torch.from_numpy(rng.integers(0, 2048, b.B)).to(dev)
-        plans = [_StepPlan(guard, ids, b.history if i == 0 else b.history.clone(), b.offsets) for i in range(4)]
+        if args.profile_packed:
+            guard = q3s.StepGuard(b.B, device=dev)
+            plans = [_StepPlan(guard, ids, b.history if i == 0 else b.history.clone(), b.offsets)
+                     for i in range(4)]
+        else:
+            lens = b.offsets[1:].cpu().long() - b.offsets[:-1].cpu().long()
+            plans = []
+            for _ in range(4):
+                rows = q3s.RowHistory.from_packed(b.history, b.offsets.cpu(), (lens + 256).tolist(), device=dev)
+                plans.append(_InPlacePlan(q3s.StepGuard(b.B, device=dev), ids, rows))
     elif args.profile_head:
         b = workloads.make_batch(cfg)
         g = torch.Generator().manual_seed(2024)

@@ -291,7 +291,9 @@ typedef struct q3s_step_desc {
   int32_t* event_run;          /* [B] ended run on RECOVERED, run on an abort, else 0 */
   int32_t* event_list;         /* [B] (row << 8) | bits for rows with any bit, ascending row */
   int32_t* event_count;        /* one int32: entries written to event_list (required with it) */
-  int32_t* error_word;         /* Q3S_DEVERR_OFFSETS on bad offsets / capacity (row skipped) */
+  int32_t* error_word;         /* Q3S_DEVERR_OFFSETS on bad offsets / capacity (row skipped);
+                                  Q3S_DEVERR_WAIT_TIMEOUT if the bounded wait of the one-launch
+                                  event-list exchange gave up (that CTA's entries not written) */
 
   /* in-place append into the capacity layout (optional; then history_out
    * must equal history and offsets_out is not used): row b's region is

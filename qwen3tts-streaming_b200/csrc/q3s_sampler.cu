@@ -378,6 +378,55 @@ int device_sm_count() {
   return n;
 }
 
+// The widest cluster step_fused_kernel<NT> gets on this device: 16 CTAs
+// (non-portable, opted in) where the device can place one, else the portable
+// 8.  Per-device cache; racing first callers store the same value.
+template <int NT>
+int fused_cluster_max() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return q3s::FUSED_MAX_CTAS;
+  int m = cache[dev].load(std::memory_order_relaxed);
+  if (m == 0) {
+    m = q3s::FUSED_MAX_CTAS;
+    const auto kern = q3s::step_fused_kernel<NT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+      cudaLaunchConfig_t lc = {};
+      lc.gridDim = dim3(q3s::FUSED_WIDE_CTAS);
+      lc.blockDim = dim3(NT);
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = q3s::FUSED_WIDE_CTAS;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      lc.attrs = at;
+      lc.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &lc) == cudaSuccess && n >= 1) m = q3s::FUSED_WIDE_CTAS;
+    }
+    (void)cudaGetLastError();  // a refused opt-in or query leaves the portable width
+    cache[dev].store(m, std::memory_order_relaxed);
+  }
+  return m;
+}
+
+template <int NT>
+cudaError_t launch_step_fused(const q3s::StepArgs& a, int rpt, int n_cta, cudaStream_t st) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>(n_cta));
+  lc.blockDim = dim3(NT);
+  lc.dynamicSmemBytes = 0;
+  lc.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = static_cast<unsigned>(n_cta);
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, q3s::step_fused_kernel<NT>, a, rpt);
+}
+
 template <int NT, int E, bool BF16, int MODE>
 q3s_status launch_cp_t(const q3s::CpArgs& a, cudaStream_t st) {
   const size_t dyn = a.bulk ? static_cast<size_t>(a.nbuf) * a.row_bytes : 0;
@@ -581,12 +630,34 @@ q3s_status q3s_step_update(const q3s_step_desc* d, void* stream) {
   a.error_word = d->error_word;
   a.history_lengths = d->history_lengths;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (append)
+  // One cluster: the narrowest CTA (128 .. 1024 threads) that covers the
+  // batch with a row per thread in 16 CTAs, so that the rows spread over as
+  // many SMs as the cluster allows (the launch is bound by the rows each SM
+  // serves); past 16 x 1024 rows, up to 4 rows a thread.
+  int fused_nt = 128;
+  while (fused_nt < 1024 && B > q3s::FUSED_WIDE_CTAS * fused_nt) fused_nt *= 2;
+  const int max_cta = fused_nt == 128   ? fused_cluster_max<128>()
+                      : fused_nt == 256 ? fused_cluster_max<256>()
+                      : fused_nt == 512 ? fused_cluster_max<512>()
+                                        : fused_cluster_max<1024>();
+  const int fused_rows = max_cta * fused_nt;
+  const bool fused = !append && B <= fused_rows * q3s::FUSED_MAX_RPT;
+  cudaError_t e = cudaSuccess;
+  if (fused) {
+    // rows per thread first, so that every CTA of the cluster has work
+    const int rpt = (B + fused_rows - 1) / fused_rows;
+    const int n_cta = (B + fused_nt * rpt - 1) / (fused_nt * rpt);
+    e = fused_nt == 128   ? launch_step_fused<128>(a, rpt, n_cta, st)
+        : fused_nt == 256 ? launch_step_fused<256>(a, rpt, n_cta, st)
+        : fused_nt == 512 ? launch_step_fused<512>(a, rpt, n_cta, st)
+                          : launch_step_fused<1024>(a, rpt, n_cta, st);
+  } else if (append) {
     q3s::step_rows_kernel<<<static_cast<unsigned>(B), q3s::APPEND_NT, 0, st>>>(a);
-  else
+  } else {
     q3s::step_lite_kernel<<<static_cast<unsigned>((B + q3s::LITE_NT - 1) / q3s::LITE_NT), q3s::LITE_NT, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess && (d->event_list || d->event_count)) {
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e == cudaSuccess && !fused && (d->event_list || d->event_count)) {
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(1);
     lc.blockDim = dim3(q3s::COMPACT_NT);

@@ -11,10 +11,16 @@
 //   history append: the packed-history form of token_counts + one_hot(id)
 //                                         scripts/export/talker_unified_modules.py:421-422
 //
-// Two launches on the caller's stream:
-//   step_lite_kernel     one thread per row: the guard, and with the capacity
-//                        layout the in-place append (history[offsets[b] +
-//                        len[b]] = ids[b], len[b] += 1): O(B) bytes a step;
+// Launches on the caller's stream:
+//   step_fused_kernel    (capacity layout or no append, B <= 65536) ONE
+//                        launch, a cluster of <= 16 CTAs of 128 .. 1024
+//                        threads: one thread per row
+//                        (up to 4) runs the guard and the in-place append
+//                        (history[offsets[b] + len[b]] = ids[b], len[b] += 1),
+//                        then the CTAs place the ordered event list through
+//                        distributed shared memory;
+//   step_lite_kernel     the same per-row work for larger batches, followed
+//                        by step_compact_kernel;
 //   step_rows_kernel     (packed layout, copied append) CTA b: thread 0 runs row b's guard (events[b],
 //                        event_run[b], state) while the CTA copies history row
 //                        b to its shifted place in the output
@@ -30,6 +36,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "q3s_device.cuh"
 #include "q3s_sampler.h"
 
 namespace q3s {
@@ -193,25 +200,28 @@ __global__ void __launch_bounds__(APPEND_NT, 8) step_rows_kernel(const StepArgs 
   if (threadIdx.x == 0) dst[n] = static_cast<int32_t>(step_id(a, b));
 }
 
-// One thread per row: the guard, and with the capacity layout the in-place
-// append of ids[b] at the end of row b inside its region [offsets[b],
-// offsets[b+1]) of history_out.  A full region gets nothing (and
-// Q3S_DEVERR_HISTORY_FULL), an inconsistent one Q3S_DEVERR_OFFSETS.
-constexpr int LITE_NT = 128;
-
-__global__ void __launch_bounds__(LITE_NT) step_lite_kernel(const StepArgs a) {
-  asm volatile("griddepcontrol.launch_dependents;");
-  const int b = static_cast<int>(blockIdx.x) * LITE_NT + static_cast<int>(threadIdx.x);
-  if (b >= a.batch) return;
+// Row b of the lite form: the guard, and with the capacity layout the
+// in-place append of ids[b] at the end of row b inside its region
+// [offsets[b], offsets[b+1]) of history_out.  A full region gets nothing (and
+// Q3S_DEVERR_HISTORY_FULL), an inconsistent one Q3S_DEVERR_OFFSETS.  Returns
+// the row's event bits.
+__device__ __forceinline__ int lite_row(const StepArgs& a, int b) {
   GuardRow r;
   guard_load(a, b, r);
+  // the row's region is read with the guard inputs, before any store, so all
+  // of the row's loads share one trip to memory
+  int64_t s = 0, e = 0;
+  int len = 0;
+  if (a.history_lengths) {
+    s = a.offsets[b];
+    e = a.offsets[b + 1];
+    len = a.history_lengths[b];
+  }
   int ev_run;
   const int bits = guard_apply(a, b, r, ev_run);
   if (a.events) a.events[b] = bits;
   if (a.event_run) a.event_run[b] = ev_run;
-  if (!a.history_lengths) return;
-  const int64_t s = a.offsets[b], e = a.offsets[b + 1];
-  const int len = a.history_lengths[b];
+  if (!a.history_lengths) return bits;
   if (s < 0 || e < s || e > a.history_out_capacity || len < 0 || s + len > e) {
     if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_OFFSETS);
   } else if (s + len == e) {
@@ -220,6 +230,111 @@ __global__ void __launch_bounds__(LITE_NT) step_lite_kernel(const StepArgs a) {
     a.history_out[s + len] = static_cast<int32_t>(r.id);
     a.history_lengths[b] = len + 1;
   }
+  return bits;
+}
+
+// One thread per row, followed by step_compact_kernel (rows beyond what one
+// cluster of step_fused_kernel covers).
+constexpr int LITE_NT = 128;
+
+__global__ void __launch_bounds__(LITE_NT) step_lite_kernel(const StepArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int b = static_cast<int>(blockIdx.x) * LITE_NT + static_cast<int>(threadIdx.x);
+  if (b >= a.batch) return;
+  lite_row(a, b);
+}
+
+// The lite form and the ordered event list in ONE launch: a cluster of up to
+// FUSED_WIDE_CTAS CTAs of NT threads, thread t of CTA c taking rows
+// (c * NT + t) * rpt ... + rpt - 1, so thread order is row order.  Each CTA
+// scans its per-thread event counts and sends its total to slot c of every
+// CTA of the cluster with st.async, which completes on the receiving CTA's
+// mbarrier (4 bytes from each CTA expected); each CTA then adds up its own
+// slots (the totals of the CTAs before it, and of all) and writes its entries
+// of event_list; CTA 0 writes event_count.  No thread fences its global
+// stores and no CTA waits for the others to finish: the only cluster barrier
+// (every CTA has started and initialised its mbarrier before any st.async
+// reaches it) is arrived at entry and waited on after the row work.  The
+// mbarrier wait is bounded; if it gives up the CTA sets
+// Q3S_DEVERR_WAIT_TIMEOUT and writes no entries.  No global scratch, no
+// second launch.
+constexpr int FUSED_MAX_CTAS = 8;    // portable cluster size
+constexpr int FUSED_WIDE_CTAS = 16;  // non-portable, where the device grants it
+constexpr int FUSED_MAX_RPT = 4;
+
+// st.async of one int32 into CTA `rank`'s copy of `slot`, completing 4 bytes
+// on that CTA's copy of `bar`.
+__device__ __forceinline__ void step_send_total(int* slot, uint64_t* bar, unsigned rank, int v) {
+  unsigned rs, rb;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rs) : "r"(smem_u32(slot)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(smem_u32(bar)), "r"(rank));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(rs), "r"(v),
+               "r"(rb)
+               : "memory");
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT, 1) step_fused_kernel(const StepArgs a, int rpt) {
+  __shared__ int warp_tot[NT / 32];
+  __shared__ int cta_tot[FUSED_WIDE_CTAS];  // slot c: the event count of CTA c
+  __shared__ __align__(8) uint64_t tot_bar;
+  const bool want_list = a.event_list || a.event_count;  // uniform over the grid
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned me = blockIdx.x, n_cta = gridDim.x;
+  if (want_list) {
+    if (tid == 0) {
+      mbar_init(&tot_bar, 1);
+      mbar_expect_tx(&tot_bar, 4u * n_cta);  // the one arrival; the bytes may land before or after it
+      fence_mbar_init();
+    }
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  }
+  const int b0 = (static_cast<int>(me) * NT + tid) * rpt;
+  uint32_t evp = 0;  // the event bits (< 2^8) of row b0 + k in byte k
+  int c = 0;
+#pragma unroll
+  for (int k = 0; k < FUSED_MAX_RPT; ++k) {
+    const int bits = k < rpt && b0 + k < a.batch ? lite_row(a, b0 + k) : 0;
+    evp |= static_cast<uint32_t>(bits) << (8 * k);
+    c += bits != 0;
+  }
+  if (!want_list) return;
+  int incl = c;  // inclusive warp scan of the per-thread counts
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int pre = incl - c, tot = 0;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) {
+    const int t = warp_tot[w];
+    pre += w < warp ? t : 0;
+    tot += t;
+  }
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started
+  if (tid < static_cast<int>(n_cta)) step_send_total(&cta_tot[me], &tot_bar, static_cast<unsigned>(tid), tot);
+  if (!mbar_wait_bounded(&tot_bar, 0)) {
+    if (tid == 0 && a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
+    return;
+  }
+  int base = 0, all = 0;
+  for (unsigned j = 0; j < n_cta; ++j) {
+    const int t = cta_tot[j];
+    base += j < me ? t : 0;
+    all += t;
+  }
+  pre += base;
+  if (a.event_list) {
+#pragma unroll
+    for (int k = 0; k < FUSED_MAX_RPT; ++k) {
+      const int bits = static_cast<int>((evp >> (8 * k)) & 0xFFu);
+      if (bits) a.event_list[pre++] = ((b0 + k) << 8) | bits;
+    }
+  }
+  if (me == 0 && tid == 0 && a.event_count) *a.event_count = all;
 }
 
 // Ordered compaction of events[0, B) into event_list ((row << 8) | bits for

@@ -142,7 +142,17 @@ def test_step_update_bad_offsets_flag_only_that_row(q3s_lib, cuda_device):
 # capacity layout: in-place append (RowHistory), O(B) bytes a step
 # ---------------------------------------------------------------------------
 
-@pytest.mark.parametrize("B,steps,max_len,cap_extra", [(128, 6, 2048, 8), (4096, 3, 4096, 4), (3, 5, 2, 2)])
+@pytest.mark.parametrize("B,steps,max_len,cap_extra", [
+    (128, 6, 2048, 8),    # config-1 sizes: one 128-thread CTA
+    (4096, 3, 4096, 4),   # config-4 sizes: one cluster of 16 x 256 threads, a row per thread
+    (3, 5, 2, 2),
+    (513, 3, 64, 2),      # five 128-thread CTAs, the last with one row
+    (1100, 2, 64, 2),     # nine 128-thread CTAs
+    (9000, 2, 64, 4),     # 1024-thread CTAs
+    (20000, 2, 16, 4),    # two rows per thread
+    (40000, 2, 8, 4),     # three rows per thread
+    (70000, 2, 8, 4),     # past one cluster: row kernel + compaction kernel
+])
 def test_in_place_append_matches_oracle(q3s_lib, cuda_device, B, steps, max_len, cap_extra):
     """Guard + in-place append over several steps against the oracle; the
     rows whose region fills up stop growing and set HISTORY_FULL."""
