@@ -235,10 +235,12 @@ q3s_status q3s_philox_seeds(const uint64_t* row_seeds, uint32_t step, uint32_t s
  * id back to the host each step (engine/backend/executor.py:532-546) and runs
  * these checks per slot in Python (engine/backend/engine_loop.py:2749-2750,
  * 2863-3080, thresholds normalised at :372-387); the count update it feeds is
- * talker_unified_modules.py:421-422.  Two kernel launches do them for all
- * rows (per-row guard + history copy, then the event compaction when asked
- * for) and leave a compact event list, so the host reads one word per step
- * (the event count) and the listed rows only when it is non-zero. */
+ * talker_unified_modules.py:421-422.  The kernels do them for all rows and
+ * leave a compact event list, so the host reads one word per step (the
+ * event count) and the listed rows only when it is non-zero: one cluster
+ * launch with the in-place append (history_lengths) or none, up to 65536
+ * rows; otherwise a per-row launch (guard + history copy) and an event
+ * compaction launch when the list or the count is asked for. */
 #define Q3S_EVT_EOS 1              /* id == eos_id: segment ends, guard skipped */
 #define Q3S_EVT_SUSPECT 2          /* loop_run reached the suspect threshold */
 #define Q3S_EVT_RECOVERED 4        /* token changed after a run >= suspect */

@@ -6,12 +6,13 @@ frame counter and the two-stage token loop guard per slot in Python
 (engine/backend/engine_loop.py:2749-2750, 2863-3080).  ``StepGuard`` keeps that
 per-slot state on the GPU -- the fields of ``EngineSegment`` (loop_token,
 loop_run, loop_max_run, loop_suspect_count, loop_recovery_count,
-engine_loop.py:184-192) and the slot's frame_idx -- and runs two launches per
-step over all rows, which also append the sampled ids to the rows' history
-(the history form of ``token_counts + one_hot(id)``,
+engine_loop.py:184-192) and the slot's frame_idx -- and runs the step over
+all rows on the device, which also appends the sampled ids to the rows'
+history (the history form of ``token_counts + one_hot(id)``,
 scripts/export/talker_unified_modules.py:421-422): in place into a
-``RowHistory`` (capacity layout, O(B) bytes a step), or as a copy of a
-packed history with one id more per row.  The host then reads one
+``RowHistory`` (capacity layout, O(B) bytes a step, one launch up to 64 K
+rows), or as a copy of a packed history with one id more per row (two
+launches).  The host then reads one
 int32 (the event count) per step, and the compact event list only when it is
 not zero.
 
