@@ -7,7 +7,8 @@
 // a stage does only what exactly-K top-k + Gumbel needs, with thread t
 // holding entries [8t, 8t+8) of the row (read from a ring of bulk-copied
 // stage rows, the producer's rotation applied on the read):
-//   1. the row maximum (warp shuffles, one exchange);
+//   1. the row maximum (one integer reduction of order-preserving keys per
+//      warp, one exchange);
 //   2. one histogram of d = max - v in bins 1/8 wide over d < 32 (shared
 //      atomics; floor((max - v) * 8) is monotone in v, so every entry at or
 //      above the K-th largest lies in the bin holding it or an earlier one);
@@ -16,8 +17,10 @@
 //      cursor, advanced atomically), so every bin is a contiguous range;
 //   4. each candidate's exact rank (value desc, index asc) = its bin's start
 //      plus its rank among the few entries of its own bin (bins are monotone
-//      in the value and equal values share a bin); the first K score v / T +
-//      noise[rank] (the noise of this stage was fetched during the previous
+//      in the value and equal values share a bin), counted over one 64-bit
+//      word per entry that orders like (value desc, index asc); the first K
+//      score v / T + noise[rank] (v / T correctly rounded through the row's
+//      reciprocal; the noise of this stage was fetched during the previous
 //      one); the argmax (lowest rank on ties).
 // Rows outside that pattern -- the K-th largest 32 or more below the maximum,
 // more than 256 entries down to its bin (massive ties) -- take the general
@@ -33,13 +36,19 @@ constexpr int CPF_NT = 256;
 constexpr int CPF_E = 8;
 constexpr int CPF_CAP = 256;  // fast-path candidates (one per thread)
 
-template <bool BF16>
-__global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
+// MINB CTAs per SM: 1 leaves the stage all the registers it wants, 2 caps
+// them (a few spilled) so that two rows share an SM.
+template <bool BF16, int MINB>
+__global__ void __launch_bounds__(CPF_NT, MINB) cp_fast_kernel(const CpArgs a) {
   constexpr int NT = CPF_NT, E = CPF_E, NW = NT / 32;
   __shared__ Scratch<NT, E> sh;
   __shared__ __align__(8) uint64_t bars[MAX_NBUF];
-  __shared__ float wmax[NW], wbs[NW];
+  __shared__ __align__(16) uint32_t wmax[NW];  // the warps' maxima as order-preserving keys
+  __shared__ float wbs[NW];
   __shared__ int wbr[NW], wbi[NW];
+  // candidate slot -> (f2key(value) << 32) | ~index: one word that orders
+  // like (value desc, index asc) when compared as an integer
+  __shared__ unsigned long long ckey[CPF_CAP];
   __shared__ int sel[2];
   extern __shared__ __align__(128) unsigned char cpf_ring[];
   const int t = static_cast<int>(threadIdx.x), w = t >> 5, lane = t & 31;
@@ -89,6 +98,11 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
     const int b = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
     int64_t prev = (a.producer == Q3S_CP_ROTATE) ? __ldg(a.ids_init + b) : 0;
     const float T = a.temperature ? __ldg(a.temperature + b) : a.temperature_default;
+    // v / T by the per-row reciprocal where that is the correctly rounded
+    // quotient (normal operands: |v| in [2^-60, 2^60], T in [2^-20, 2^20]),
+    // else by the division itself
+    const bool t_ok = T >= 0x1p-20f && T <= 0x1p20f;
+    const float rT = __frcp_rn(t_ok ? T : 1.0f);
     for (int j = 0; j < S; ++j) {
       const int g = i * S + j;
       const int shift = (a.producer == Q3S_CP_ROTATE) ? norm_shift(prev, V) : 0;
@@ -123,16 +137,22 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
         }
       }
 
-      // 1. the row maximum
-      float m = x[0];
+      // 1. the row maximum: the thread's (NaN dropped), then one integer
+      //    reduction of order-preserving keys per warp (key 0, below every
+      //    key, for a thread whose entries are all NaN)
+      float tm = x[0];
 #pragma unroll
-      for (int e = 1; e < E; ++e) m = fmaxf(m, x[e]);
-      m = warp_max_f(m);
-      if (lane == 0) wmax[w] = m;
+      for (int e = 1; e < E; ++e) tm = fmaxf(tm, x[e]);
+      const uint32_t wk_max = __reduce_max_sync(FULL, tm != tm ? 0u : f2key(tm));
+      if (lane == 0) wmax[w] = wk_max;
       __syncthreads();  // (1)
-      m = wmax[0];
-#pragma unroll
-      for (int k = 1; k < NW; ++k) m = fmaxf(m, wmax[k]);
+      float m;
+      {
+        static_assert(NW == 8, "two 16-byte reads of the warps' keys");
+        const uint4 k0 = reinterpret_cast<const uint4*>(wmax)[0], k1 = reinterpret_cast<const uint4*>(wmax)[1];
+        const uint32_t mk = max(max(max(k0.x, k0.y), max(k0.z, k0.w)), max(max(k1.x, k1.y), max(k1.z, k1.w)));
+        m = key2f(mk);  // NaN when no warp had a number: every bin test fails, the row takes the core
+      }
       // 2. histogram of floor((m - v) * 8) over d < 32 (each entry's bin
       //    kept; 256 = beyond)
       int eb[E];
@@ -226,7 +246,7 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
         if (eb[e] <= bK) {
           const uint32_t slot = atomicAdd(&sh.hist[0][eb[e]], 1u);
           sh.xs[slot] = x[e];
-          sh.cand[slot] = make_uint4(0u, static_cast<uint32_t>(v0 + e), static_cast<uint32_t>(eb[e]), 0u);
+          ckey[slot] = (static_cast<unsigned long long>(f2key(x[e])) << 32) | ~static_cast<uint32_t>(v0 + e);
         }
       __syncthreads();  // (4)
       // 4. exact rank (value desc, index asc): the bins are monotone in the
@@ -238,18 +258,18 @@ __global__ void __launch_bounds__(CPF_NT) cp_fast_kernel(const CpArgs a) {
       int br = 0x7fffffff, bi = 0;
       if (t < n) {
         const float vp = sh.xs[t];
-        const uint4 me = sh.cand[t];
-        const uint32_t k = me.z;
+        const unsigned long long me = ckey[t];
+        // the bin again, by the same arithmetic as in 2.
+        const uint32_t k = static_cast<uint32_t>(__fmul_rn(__fsub_rn(m, vp), 8.0f));
         const uint32_t start = k ? sh.hist[0][k - 1] : 0u, end = sh.hist[0][k];
         int r = static_cast<int>(start);
-        for (uint32_t q = start; q < end; ++q) {
-          const float f = sh.xs[q];
-          r += (f > vp) || (f == vp && sh.cand[q].y < me.y);
-        }
+        for (uint32_t q = start; q < end; ++q) r += ckey[q] > me;
         if (r < K) {
-          bs = __fadd_rn(__fdiv_rn(vp, T), sh.noise[(g & 1) * CPF_CAP + r]);
+          const float av = fabsf(vp);
+          const float sc = t_ok && av >= 0x1p-60f && av <= 0x1p60f ? div_rn_row(vp, T, rT) : __fdiv_rn(vp, T);
+          bs = __fadd_rn(sc, sh.noise[(g & 1) * CPF_CAP + r]);
           br = r;
-          bi = static_cast<int>(me.y);
+          bi = static_cast<int>(~static_cast<uint32_t>(me));
         }
       }
       // argmax (score desc, rank asc) by two warp reductions: the largest

@@ -49,6 +49,21 @@ Q3S_DEV float key2f(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// x / d rounded to nearest even, for a per-row divisor d with r = RN(1/d):
+// two residual corrections of q0 = RN(x r) (Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990; Cornea, Harrison and Tang, "Scientific Computing on
+// Itanium-based Systems", 2002): the first makes the quotient faithful, and
+// with r the correctly rounded reciprocal the second, RN(q1 + r RN(x - d q1)),
+// is the correctly rounded quotient while x, d, the quotient and the
+// residuals stay normal (|x| and x/d within [2^-80, 2^100], d within
+// [2^-20, 2^20]).  Finite x only.
+Q3S_DEV float div_rn_row(float x, float d, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q1 = __fmaf_rn(__fmaf_rn(-q0, d, x), r, q0);
+  return __fmaf_rn(__fmaf_rn(-q1, d, x), r, q1);
+}
+
 Q3S_DEV float bf16_bits_to_f32(uint32_t h16) { return __uint_as_float(h16 << 16); }
 
 // torch.argmax order: NaN beats everything (first NaN wins), then larger

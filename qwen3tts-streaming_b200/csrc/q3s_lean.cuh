@@ -84,21 +84,6 @@ Q3S_DEV float ex2(float x) {
 // Byte i (0..7) of an 8-byte word is nonzero.
 Q3S_DEV bool byte_set(const uint2& w, int i) { return ((i < 4 ? w.x : w.y) & (0xffu << (8 * (i & 3)))) != 0u; }
 
-// x / d rounded to nearest even, for a per-row divisor d with r = RN(1/d):
-// two residual corrections of q0 = RN(x r) (Markstein, "Computation of
-// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
-// Dev. 34(1), 1990; Cornea, Harrison and Tang, "Scientific Computing on
-// Itanium-based Systems", 2002): the first makes the quotient faithful, and
-// with r the correctly rounded reciprocal the second, RN(q1 + r RN(x - d q1)),
-// is the correctly rounded quotient while x, d, the quotient and the
-// residuals stay normal (|x| and x/d within [2^-80, 2^100], d within
-// [2^-20, 2^20]).  Finite x only.
-Q3S_DEV float div_rn_row(float x, float d, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float q1 = __fmaf_rn(__fmaf_rn(-q0, d, x), r, q0);
-  return __fmaf_rn(__fmaf_rn(-q1, d, x), r, q1);
-}
-
 // div_rn_row on the two lanes of packed fp32x2 arithmetic (the same roundings).
 Q3S_DEV float2 div2_rn_row(float2 x, float d, float r) {
   const float2 dd = make_float2(-d, -d), rr = make_float2(r, r);

@@ -902,22 +902,28 @@ q3s_status q3s_sample_cp_frame(const q3s_cp_frame_desc* d, void* stream) {
   if (a.mode == Q3S_DRAW_GUMBEL && a.noise && a.bulk && V <= q3s::CPF_NT * q3s::CPF_E && a.K <= q3s::CPF_CAP &&
       policy != Q3S_POLICY_CTA) {
     const size_t dyn = static_cast<size_t>(a.nbuf) * a.row_bytes;
-    auto kern = bf16 ? q3s::cp_fast_kernel<true> : q3s::cp_fast_kernel<false>;
+    // one CTA per SM holds the whole register budget of the stage (rows that
+    // fit on the SMs at once); with more rows than SMs two CTAs share an SM
+    // (fewer registers each), so that two rows' stage chains interleave
+    const bool wide = a.B > device_sm_count();
+    auto kern = bf16 ? (wide ? q3s::cp_fast_kernel<true, 2> : q3s::cp_fast_kernel<true, 1>)
+                     : (wide ? q3s::cp_fast_kernel<false, 2> : q3s::cp_fast_kernel<false, 1>);
+    const int ki = (bf16 ? 2 : 0) + (wide ? 1 : 0);
     {
       // the ring may pass the 48 KB default: opt in (idempotent per kernel
       // and device; the value only ever grows)
-      static std::atomic<int> granted[2][64];
+      static std::atomic<int> granted[4][64];
       int dev = 0;
       cudaGetDevice(&dev);
       const bool known = dev >= 0 && dev < 64;
-      if (!known || granted[bf16][dev].load(std::memory_order_acquire) < static_cast<int>(dyn)) {
+      if (!known || granted[ki][dev].load(std::memory_order_acquire) < static_cast<int>(dyn)) {
         const cudaError_t e =
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
         if (e != cudaSuccess) return fail(Q3S_ERR_CUDA, "q3s_sample_cp_frame smem attribute: %s", cudaGetErrorString(e));
         if (known) {
-          int cur = granted[bf16][dev].load(std::memory_order_relaxed);
+          int cur = granted[ki][dev].load(std::memory_order_relaxed);
           while (cur < static_cast<int>(dyn) &&
-                 !granted[bf16][dev].compare_exchange_weak(cur, static_cast<int>(dyn), std::memory_order_release)) {
+                 !granted[ki][dev].compare_exchange_weak(cur, static_cast<int>(dyn), std::memory_order_release)) {
           }
         }
       }

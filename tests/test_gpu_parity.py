@@ -363,16 +363,25 @@ def test_cp_frame_equals_fifteen_single_stage_launches(cuda_device, q3s_lib):
     np.testing.assert_array_equal(torch.stack(outs, 1).cpu().numpy(), frame.cpu().numpy())
 
 
-@pytest.mark.parametrize("case", ["ties", "spread", "mixed", "fp32"])
+@pytest.mark.parametrize("case", ["ties", "spread", "mixed", "fp32", "tiny", "extreme_t", "wide"])
 def test_cp_frame_fast_path_and_its_fallbacks(cuda_device, q3s_lib, case):
     """The Gumbel frame kernel (auto policy) against the oracle chain and the
     CTA-per-row frame kernel, on rows that leave its fast pattern: massive
     ties (more than 256 entries down to the K-th's bin) and widely spread
     values (the K-th 32 or more below the maximum), alone and mixed with
-    ordinary rows, bf16 and fp32."""
-    rng = np.random.default_rng({"ties": 1, "spread": 2, "mixed": 3, "fp32": 4}[case])
-    S, B, V = 5, 40, 2048
+    ordinary rows, bf16 and fp32; on candidates whose v / T leaves the
+    reciprocal's window (tiny and signed-zero values, temperatures outside
+    [2^-20, 2^20]); and on more rows than SMs (two CTAs per SM)."""
+    rng = np.random.default_rng({"ties": 1, "spread": 2, "mixed": 3, "fp32": 4, "tiny": 5, "extreme_t": 6,
+                                 "wide": 7}[case])
+    S, B, V = 5, (400 if case == "wide" else 40), 2048
     base = (rng.standard_normal((S, B, V)) * 2.5).astype(np.float32)
+    if case == "tiny":
+        # rows far below zero with 80 planted entries at tiny magnitudes and
+        # both zeros, all of them inside the top 50's reach
+        base[:, ::2, :] -= 30.0
+        tiny = np.array([1e-20, -1e-20, 3e-19, -7e-22, 0.0, -0.0, 2e-30, -5e-25], np.float32)
+        base[:, ::2, 100:180] = np.resize(tiny, 80)
     if case in ("ties", "mixed"):
         rows = slice(None) if case == "ties" else slice(0, B, 3)
         base[:, rows, :] = np.round(base[:, rows, :] * 2) / 2  # a few hundred entries share each top value
@@ -387,6 +396,9 @@ def test_cp_frame_fast_path_and_its_fallbacks(cuda_device, q3s_lib, case):
         base = bt.float().numpy()
     init = rng.integers(0, V, B)
     T = rng.uniform(0.6, 1.0, B).astype(np.float32)
+    if case == "extreme_t":
+        T[::3] = 1e-7
+        T[1::3] = 3e6
     u = rng.random((B, S, 50)).astype(np.float32)
     from q3s.philox import gumbel_from_uniforms
     noise = gumbel_from_uniforms(u)
