@@ -5,7 +5,7 @@
 //
 // A frame is latency-bound (one row per SM at the engine's batch sizes), so
 // a stage does only what exactly-K top-k + Gumbel needs, with thread t
-// holding entries [8t, 8t+8) of the row (read from a ring of bulk-copied
+// holding entries t, t + 256, ... of the row (read from a ring of bulk-copied
 // stage rows, the producer's rotation applied on the read):
 //   1. the row maximum (one integer reduction of order-preserving keys per
 //      warp, one exchange);
@@ -24,7 +24,8 @@
 //      one); the argmax (lowest rank on ties).
 // Rows outside that pattern -- the K-th largest 32 or more below the maximum,
 // more than 256 entries down to its bin (massive ties) -- take the general
-// CTA sampler core, which holds the row in the same register layout.
+// CTA sampler core on the row re-read in that core's layout (thread t holding
+// entries [8t, 8t+8)).
 #pragma once
 
 #include "q3s_args.cuh"
@@ -117,25 +118,30 @@ __global__ void __launch_bounds__(CPF_NT, MINB) cp_fast_kernel(const CpArgs a) {
         }
         return;
       }
-      // every thread is past the previous stage: refill its slot, prefetch
-      // the next stage's noise
-      if (t == 0 && g > 0 && g - 1 + a.nbuf < nitems) issue(g - 1 + a.nbuf);
+      // every thread is past the previous stage: prefetch the next stage's
+      // noise (its slot is refilled below, off the critical path)
       const float nz_next = fetch_noise(g + 1);
       const unsigned char* row = cpf_ring + static_cast<size_t>(slot) * a.row_bytes;
-      float x[E];
-      uint32_t vmask = 0;
+      // entries v = t + NT e, e < E (the producer's rotation applied on the
+      // read): a warp's loads are consecutive words, free of bank conflicts
+      auto load_row = [&](float (&xr)[E], uint32_t& vm, int first, int step) {
+        vm = 0;
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int v = v0 + e;
-        x[e] = -INFINITY;
-        if (v < V) {
-          int q = v + shift;
-          q -= q >= V ? V : 0;
-          x[e] = BF16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(row)[q])
-                      : reinterpret_cast<const float*>(row)[q];
-          vmask |= 1u << e;
+        for (int e = 0; e < E; ++e) {
+          const int v = first + step * e;
+          xr[e] = -INFINITY;
+          if (v < V) {
+            int q = v + shift;
+            q -= q >= V ? V : 0;
+            xr[e] = BF16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(row)[q])
+                         : reinterpret_cast<const float*>(row)[q];
+            vm |= 1u << e;
+          }
         }
-      }
+      };
+      float x[E];
+      uint32_t vmask;
+      load_row(x, vmask, t, NT);
 
       // 1. the row maximum: the thread's (NaN dropped), then one integer
       //    reduction of order-preserving keys per warp (key 0, below every
@@ -163,6 +169,8 @@ __global__ void __launch_bounds__(CPF_NT, MINB) cp_fast_kernel(const CpArgs a) {
         if (eb[e] < 256) atomicAdd(&sh.hist[0][eb[e]], 1u);
       }
       __syncthreads();  // (2)
+      // while warp 0 scans: refill the previous stage's slot
+      if (t == 32 && g > 0 && g - 1 + a.nbuf < nitems) issue(g - 1 + a.nbuf);
       if (w == 0) {
         // the bin holding the K-th largest and the count through it; every
         // bin's count becomes its exclusive prefix (the placement cursor)
@@ -211,9 +219,11 @@ __global__ void __launch_bounds__(CPF_NT, MINB) cp_fast_kernel(const CpArgs a) {
       const int bK = sel[0], n = sel[1];
       int id, flags = 0;
       if (bK >= 256 || n > CPF_CAP) {
-        // outside the fast pattern: the general CTA core on the same
-        // registers, the histogram (now cursors) back to zero first
+        // outside the fast pattern: the general CTA core, on the row again in
+        // its layout (thread t holds entries [E t, E t + E)), the histogram
+        // (now cursors) back to zero first
         for (int i = t; i < NBINS; i += NT) sh.hist[0][i] = 0u;
+        load_row(x, vmask, v0, 1);
         __syncthreads();
         RowCfg c;
         c.mode = Q3S_DRAW_GUMBEL;
@@ -246,7 +256,7 @@ __global__ void __launch_bounds__(CPF_NT, MINB) cp_fast_kernel(const CpArgs a) {
         if (eb[e] <= bK) {
           const uint32_t slot = atomicAdd(&sh.hist[0][eb[e]], 1u);
           sh.xs[slot] = x[e];
-          ckey[slot] = (static_cast<unsigned long long>(f2key(x[e])) << 32) | ~static_cast<uint32_t>(v0 + e);
+          ckey[slot] = (static_cast<unsigned long long>(f2key(x[e])) << 32) | ~static_cast<uint32_t>(t + NT * e);
         }
       __syncthreads();  // (4)
       // 4. exact rank (value desc, index asc): the bins are monotone in the
