@@ -108,18 +108,12 @@ __global__ void __launch_bounds__(CPF_NT, MINB) cp_fast_kernel(const CpArgs a) {
       const int g = i * S + j;
       const int shift = (a.producer == Q3S_CP_ROTATE) ? norm_shift(prev, V) : 0;
       const int slot = g % a.nbuf;
+      // each thread waits for the row itself; whether any wait gave up is
+      // agreed on at barrier (1), the first the stage takes (nothing before
+      // it stores to shared memory but the warps' maxima)
       const bool ok = mbar_wait_bounded(&bars[slot], static_cast<uint32_t>((g / a.nbuf) & 1));
-      if (__syncthreads_or(!ok)) {  // (barrier 0) give up: report, wait (bounded) for copies in flight
-        if (t == 0) {
-          if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
-          const int issued = g == 0 ? a.nbuf : a.nbuf - 1;
-          for (int h = g; h < min(g + issued, nitems); ++h)
-            (void)mbar_wait_bounded(&bars[h % a.nbuf], static_cast<uint32_t>((h / a.nbuf) & 1));
-        }
-        return;
-      }
-      // every thread is past the previous stage: prefetch the next stage's
-      // noise (its slot is refilled below, off the critical path)
+      // prefetch the next stage's noise (the previous stage's slot is
+      // refilled below, off the critical path)
       const float nz_next = fetch_noise(g + 1);
       const unsigned char* row = cpf_ring + static_cast<size_t>(slot) * a.row_bytes;
       // entries v = t + NT e, e < E (the producer's rotation applied on the
@@ -151,7 +145,15 @@ __global__ void __launch_bounds__(CPF_NT, MINB) cp_fast_kernel(const CpArgs a) {
       for (int e = 1; e < E; ++e) tm = fmaxf(tm, x[e]);
       const uint32_t wk_max = __reduce_max_sync(FULL, tm != tm ? 0u : f2key(tm));
       if (lane == 0) wmax[w] = wk_max;
-      __syncthreads();  // (1)
+      if (__syncthreads_or(!ok)) {  // (1) a wait gave up: report, wait (bounded) for copies in flight
+        if (t == 0) {
+          if (a.error_word) atomicOr(a.error_word, Q3S_DEVERR_WAIT_TIMEOUT);
+          const int issued = g == 0 ? a.nbuf : a.nbuf - 1;
+          for (int h = g; h < min(g + issued, nitems); ++h)
+            (void)mbar_wait_bounded(&bars[h % a.nbuf], static_cast<uint32_t>((h / a.nbuf) & 1));
+        }
+        return;
+      }
       float m;
       {
         static_assert(NW == 8, "two 16-byte reads of the warps' keys");
