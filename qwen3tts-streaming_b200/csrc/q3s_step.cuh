@@ -256,8 +256,10 @@ __global__ void __launch_bounds__(LITE_NT) step_lite_kernel(const StepArgs a) {
 // (every CTA has started and initialised its mbarrier before any st.async
 // reaches it) is arrived at entry and waited on after the row work.  The
 // mbarrier wait is bounded; if it gives up the CTA sets
-// Q3S_DEVERR_WAIT_TIMEOUT and writes no entries.  No global scratch, no
-// second launch.
+// Q3S_DEVERR_WAIT_TIMEOUT and writes no entries.  (Every CTA sends its totals
+// unconditionally right after the cluster barrier, with no wait in between,
+// so a late send, not a missing one, is the only way to reach that branch.)
+// No global scratch, no second launch.
 constexpr int FUSED_MAX_CTAS = 8;    // portable cluster size
 constexpr int FUSED_WIDE_CTAS = 16;  // non-portable, where the device grants it
 constexpr int FUSED_MAX_RPT = 4;
