@@ -4,6 +4,7 @@ Run in a container where the reference checkout is available (it is not on
 the GPU box; the fixtures it writes are committed instead):
 
     python tests/golden/make_golden.py --reference /path/to/Qwen3TTS-Streaming
+    python tests/golden/make_golden.py --reference ... --time   # CPU baseline (i)
 
 Cases (inputs are seeded synthetic tensors; outputs come from the reference):
 
@@ -268,6 +269,78 @@ def case_icdf_hf_extended(seed, B):
                 sort_tie_rows=sort_tie)
 
 
+def time_reference(configs=(1, 4), iters=50, warmup=5):
+    """CPU baseline (i): the reference's own sampler fragment timed on this
+    host -- ``TalkerUnifiedFusedONNX.forward`` with the stub modules on each
+    codebook-0 config's synthetic inputs (logits, token_counts built from the
+    rows' histories, Gumbel noise of the shared uniforms, per-row temperature
+    and penalty), and ``CodePredictorUnrolled._select_token`` 15 times in
+    sequence on config 2's stage logits.  p50 over ``iters`` steps after
+    ``warmup``; one JSON line per config."""
+    import json
+    import platform
+    import time
+
+    from talker_unified_modules import TalkerUnifiedFusedONNX
+    from utils import CodePredictorUnrolled
+
+    from q3s import workloads
+
+    cpu = platform.processor() or platform.machine()
+    try:
+        with open("/proc/cpuinfo") as fh:
+            cpu = next((ln.split(":", 1)[1].strip() for ln in fh if ln.startswith("model name")), cpu)
+    except OSError:
+        pass
+    host = dict(cores=os.cpu_count(), torch_threads=torch.get_num_threads(), cpu=cpu)
+
+    def p50(fn):
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(iters):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return float(np.median(ts))
+
+    for cfg in configs:
+        b = workloads.make_batch(cfg)
+        B, Vb = b.B, b.V
+        logits = b.logits.float().reshape(B, 1, Vb)
+        hist, offs = b.history.numpy(), b.offsets.numpy().astype(np.int64)
+        tc = torch.from_numpy(counts_from(hist, offs, B, Vb))
+        fused = TalkerUnifiedFusedONNX(_StubTalker(logits), _StubCP(), _StubSum(), vocab_size=Vb,
+                                       codec_eos_token_id=EOS).eval()
+        args_ = (torch.zeros(B, 1, 4), torch.zeros(B, 3, 1, 1, dtype=torch.long), tc, b.gumbel_noise.float(),
+                 torch.zeros(B, 15, K), b.temperature.reshape(B, 1), b.penalty.reshape(B, 1))
+
+        def step():
+            with torch.no_grad():
+                fused(*args_)
+
+        t = p50(step)
+        print(json.dumps({"baseline": "(i) reference TalkerUnifiedFusedONNX.forward, stub modules",
+                          "config": cfg, "B": B, "V": Vb, "p50_step_us": round(1e6 * t, 1),
+                          "tokens_per_s": round(B / t, 1), "iters": iters, **host}), flush=True)
+    f = workloads.make_cp_frame()
+    S, B = f.base.shape[0], f.base.shape[1]
+    stages = [f.base[j].float().reshape(B, 1, -1) for j in range(S)]
+    T = f.temperature.reshape(B, 1)
+    fake_self = types.SimpleNamespace(logits_topk=K)
+
+    def frame():
+        with torch.no_grad():
+            for j in range(S):
+                CodePredictorUnrolled._select_token(fake_self, stages[j], temperature=T,
+                                                    gumbel_noise=f.gumbel_noise[:, j, :])
+
+    t = p50(frame)
+    print(json.dumps({"baseline": "(i) reference CodePredictorUnrolled._select_token x 15", "config": 2,
+                      "B": B, "V": int(stages[0].shape[-1]), "p50_frame_us": round(1e6 * t, 1),
+                      "tokens_per_s": round(B * S / t, 1), "iters": iters, **host}), flush=True)
+
+
 def save(name, d):
     d = {k: v for k, v in d.items() if v is not None}
     np.savez_compressed(HERE / f"{name}.npz", **d)
@@ -278,10 +351,17 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("Q3S_REFERENCE"),
                     help="reference checkout (default: $Q3S_REFERENCE)")
+    ap.add_argument("--time", action="store_true",
+                    help="instead of writing fixtures, time the reference's sampler fragment on this host "
+                         "(CPU baseline (i)) with every host thread")
     args = ap.parse_args()
     if not args.reference:
         ap.error("give --reference <reference checkout> or set Q3S_REFERENCE")
     ref_paths(Path(args.reference))
+    if args.time:
+        torch.set_num_threads(os.cpu_count() or 1)
+        time_reference()
+        return
     torch.set_num_threads(1)
     save("gumbel_cb0_f32", case_gumbel(11, 8, bf16=False))
     save("gumbel_cb0_bf16", case_gumbel(12, 16, bf16=True))
